@@ -1,0 +1,30 @@
+// Internal interface of the HPL module (kernels in hpl_kernels.cu, panel in
+// panel.cu, driver in hpl_single.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace chpl {
+
+// rows (or columns) of an n-long dimension owned by process coordinate p of P
+// under block-cyclic distribution with block nb (block i lives on i % P).
+static inline int64_t local_extent(int64_t n, int64_t nb, int P, int p)
+{
+    const int64_t nblk = n / nb, rem = n % nb;
+    int64_t ext = (nblk / P + (p < nblk % P ? 1 : 0)) * nb;
+    if (rem && nblk % P == p) ext += rem;
+    return ext;
+}
+
+int matgen(cudaStream_t st, double* A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0, int64_t ncg,
+           uint64_t seed);
+size_t laswp_work_bytes(int64_t nswaps);
+int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work);
+int laswp_apply(cudaStream_t st, double* A, size_t lda, int64_t c0, int64_t ncols, int64_t nswaps, const void* work);
+int ipiv_to_abs(cudaStream_t st, const int64_t* rel, int64_t n, int64_t base, int64_t* out);
+int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid);
+int hpl_read_clear_status(int* st);
+
+}  // namespace chpl

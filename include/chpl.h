@@ -1,0 +1,205 @@
+/*
+ * chpl.h -- C ABI of libchpl (chpl_b200), a B200-native (sm_100a) HPL engine.
+ *
+ * Conventions: every entry point returns an int status (CHPL_OK = 0, negative
+ * on error; chpl_last_error_string() describes the last failure on the calling
+ * thread).  Nothing aborts the process.  Matrices are FP64 column-major.
+ * Device pointers are plain pointers; `stream` is a cudaStream_t passed as
+ * void* (NULL = legacy default stream).  Calls are asynchronous on `stream`
+ * unless stated otherwise.  Buffers are owned by the caller.
+ *
+ * Each declaration names the interface of Koyingtw/CHPL (file:line inside the
+ * reference project) that it replaces.
+ */
+#ifndef CHPL_H
+#define CHPL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHPL_OK 0
+#define CHPL_ERR_INVALID (-1)     /* bad argument */
+#define CHPL_ERR_CUDA (-2)        /* CUDA runtime / driver error */
+#define CHPL_ERR_TIMEOUT (-3)     /* a bounded device-side wait ran out */
+#define CHPL_ERR_WORKSPACE (-4)   /* workspace or device memory too small */
+#define CHPL_ERR_UNSUPPORTED (-5) /* valid request this build does not serve */
+#define CHPL_ERR_SINGULAR (-6)    /* exact zero pivot */
+#define CHPL_ERR_NCCL (-7)        /* NCCL error */
+#define CHPL_ERR_NO_DEVICE (-8)   /* no sm_100 device */
+
+#define CHPL_OP_N 0
+#define CHPL_OP_T 1
+
+/* Human-readable description of the last error on this host thread. */
+const char *chpl_last_error_string(void);
+/* Library version string, e.g. "chpl_b200 0.1 (sm_100a)". */
+const char *chpl_version(void);
+/* Sticky device-side error (timeouts inside kernels) of the current device:
+ * writes it to *status and clears it.  Synchronizes the device. */
+int chpl_device_status(int *status);
+
+/* ------------------------------------------------------------------------ */
+/* Ozaki scheme II emulated DGEMM (trailing-matrix update)                   */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Workspace bytes for chpl_oz2_gemm.  Replaces
+ *   gemmul8::workSize<false, gemmul8::Backend::INT8>(m, n, k, num_moduli,
+ *       enable_skip_scalA, enable_skip_scalB, &wsA, &wsB)
+ * called at src/chpl_single.cu:367-369, src/chpl_p2.cu:755-757,
+ * src/chpl_p4.cu:919-921.
+ * *work_bytes: size of `work` when workA/workB are NULL (all parts inside);
+ * *wsA / *wsB (may be NULL): sizes of the A part (int8 residues + scales of
+ * op(A)) and B part, which the caller may instead place in workA / workB.
+ * num_moduli in [2, 16]; k <= 131071.
+ */
+int chpl_oz2_worksize(size_t m, size_t n, size_t k, unsigned num_moduli, int enable_skip_scalA,
+                      int enable_skip_scalB, size_t *work_bytes, size_t *wsA, size_t *wsB);
+
+/*
+ * C = alpha * op(A) * op(B) + beta * C, FP64 emulated with int8 tensor cores
+ * (Ozaki scheme II, num_moduli moduli).  Replaces
+ *   gemmul8::gemm<double, gemmul8::Backend::INT8>(handle, opA, opB, m, n, k,
+ *       alpha, A, lda, B, ldb, beta, C, ldc, num_moduli, fastmode, work,
+ *       workA, workB, enable_skip_scalA, enable_skip_scalB, skip_scalA,
+ *       skip_scalB)
+ * called at src/chpl_single.cu:641-649, src/chpl_p2.cu:1674-1683,
+ * src/chpl_p4.cu:2340-2350 and 2362-2373 (the stream replaces the cuBLAS
+ * handle, whose stream the reference sets at src/chpl_p2.cu:760-761).
+ * skip_scalA = 1 reuses the residues of op(A) left in the A part by the
+ * previous call with the same A, m, k, num_moduli (the per-panel reuse of
+ * src/chpl_p2.cu:1642-1643,1684); likewise skip_scalB.
+ * Scaling: power-of-two row/column scales from Cauchy-Schwarz bounds (the
+ * 2-norms of the rows of op(A) and columns of op(B)), the fast mode of the
+ * published method.  fastmode == 0 is accepted and uses the same rule (this
+ * build has no separate accurate mode).
+ * phase_seconds (NULL or double[4]): when non-NULL the call synchronizes and
+ * reports {split, int8 GEMM + fused mod/CRT/unscale, 0, 0} in seconds --
+ * the four phase times gemmul8::gemm returns (src/chpl_single.cu:651).
+ */
+int chpl_oz2_gemm(void *stream, int opA, int opB, size_t m, size_t n, size_t k, const double *alpha,
+                  const double *A, size_t lda, const double *B, size_t ldb, const double *beta, double *C,
+                  size_t ldc, unsigned num_moduli, int fastmode, void *work, void *workA, void *workB,
+                  int enable_skip_scalA, int enable_skip_scalB, int skip_scalA, int skip_scalB,
+                  double *phase_seconds);
+
+/*
+ * Pieces of chpl_oz2_gemm, exposed for verification (no reference
+ * counterpart: GEMMul8 keeps them internal).  Layouts:
+ *   rows residues  res[(l * ld_vec + i) * ld_k + h], i < m, h < k, l < L
+ *   (K-major; ld_vec >= m, ld_k >= k, ld_k % 128 == 0; padding written 0),
+ *   shift[i] such that op(A)[i,h] * 2^shift[i] rounds to the integer image.
+ * chpl_oz2_split_rows: op(A) (m x k) -> residues of its rows.
+ * chpl_oz2_split_cols: op(B) (k x n) -> residues of its columns.
+ * chpl_oz2_products: per-modulus exact int32 products of split residues,
+ *   P[l * ldp * n + i + j * ldp] = sum_h ra[l][i][h] * rb[l][j][h], through
+ *   the same tcgen05 GEMM kernel as chpl_oz2_gemm (raw epilogue).
+ *   ra/rb must have ld_vec multiples of 128 / 256 respectively.
+ */
+int chpl_oz2_split_rows(void *stream, int opA, size_t m, size_t k, const double *A, size_t lda,
+                        unsigned num_moduli, int8_t *res, size_t ld_vec, size_t ld_k, int32_t *shift,
+                        void *tmp);
+int chpl_oz2_split_cols(void *stream, int opB, size_t k, size_t n, const double *B, size_t ldb,
+                        unsigned num_moduli, int8_t *res, size_t ld_vec, size_t ld_k, int32_t *shift,
+                        void *tmp);
+/* bytes of `tmp` the split functions need for num_vectors vectors */
+size_t chpl_oz2_split_tmp_bytes(size_t num_vectors);
+int chpl_oz2_products(void *stream, size_t m, size_t n, size_t k, unsigned num_moduli, const int8_t *ra,
+                      size_t lda_vec, const int8_t *rb, size_t ldb_vec, size_t ld_k, int32_t *P, size_t ldp);
+/* scaling exponents (alpha, beta) used for num_moduli (host-only query) */
+int chpl_oz2_shift_bits(unsigned num_moduli, size_t k, int *alpha_bits, int *beta_bits);
+
+/* ------------------------------------------------------------------------ */
+/* HPL building blocks                                                       */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * A[i + j*lda] = elem(seed, (grow(i)) * ncg + gcol(j)) for an m x n block,
+ * elem = chpl_elem of src/chpl_p2.cu:66-73 (SplitMix64, [-0.5, 0.5)).
+ * Global row of local row i: row0 + i (block-cyclic maps use the grid call
+ * chpl_matgen_cyclic).  Replaces matgen2d_kernel (src/chpl_p2.cu:76-87).
+ */
+int chpl_matgen(void *stream, double *A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0,
+                int64_t ncg, uint64_t seed);
+/* Block-cyclic local piece of the N x (N+1) system for grid coordinate
+ * (pr, qc) of a P x Q grid with block NB (src/chpl_p2.cu:615-626,951-957). */
+int chpl_matgen_cyclic(void *stream, double *A, size_t lda, int64_t N, int64_t NB, int P, int Q, int pr,
+                       int qc, uint64_t seed);
+
+/*
+ * Row interchanges, LAPACK dlaswp semantics on columns [0, ncols) of A:
+ * for i = k1..k2-1 (in order) swap rows i and ipiv[i] (0-based, absolute).
+ * Applied as one gather/scatter of the net permutation built on the device
+ * (no host synchronization).  Replaces apply_swaps + row_gather/scatter
+ * (src/chpl_single.cu:489-518, 108-134).  `work` >= chpl_laswp_work_bytes.
+ */
+size_t chpl_laswp_work_bytes(int64_t nrows, int64_t nswaps);
+int chpl_laswp(void *stream, double *A, size_t lda, int64_t ncols, int64_t k1, int64_t k2,
+               const int64_t *ipiv, int64_t nrows, void *work);
+
+/*
+ * FP64 LU with partial pivoting of an m x n panel (m >= n), in place:
+ * recursive, warp-shuffle pivot search.  ipiv (device, n entries) receives
+ * 0-based pivot rows relative to the panel, LAPACK order.  info (device int)
+ * receives 0 or the 1-based column of the first exact zero pivot.
+ * Replaces cusolverDnXgetrf of the panel (src/chpl_single.cu:668-679).
+ */
+size_t chpl_panel_getrf_work_bytes(int64_t m, int64_t n);
+int chpl_panel_getrf_f64(void *stream, int64_t m, int64_t n, double *A, size_t lda, int64_t *ipiv,
+                         int *info, void *work);
+
+/*
+ * HPL scaled residual of x (device, N) for the generated N x (N+1) system
+ * (regenerated on the fly, b = column N): ||Ax-b||_oo /
+ * (eps*(||A||_oo*||x||_oo+||b||_oo)*N), eps = 2^-53.  Synchronizes.
+ * Replaces the verification of src/chpl_single.cu:762-817 /
+ * src/chpl_p2.cu:1886-1932.
+ */
+int chpl_residual(void *stream, int64_t N, uint64_t seed, const double *x, double *resid);
+
+/* ------------------------------------------------------------------------ */
+/* HPL solver                                                                */
+/* ------------------------------------------------------------------------ */
+typedef struct chpl_hpl_config {
+    int64_t N;          /* order (HPL.dat line 6) */
+    int64_t NB;         /* panel width (HPL.dat line 8) */
+    int P, Q;           /* process grid (rank = P*qc + pr) */
+    int moduli;         /* CHPL2D_G8_MODULI / HPLS_G8_MODULI */
+    int emulate;        /* CHPL2D_G8 / HPLS_BACKEND=gemmul8: 1 = Ozaki-II update, 0 = FP64 */
+    int fast;           /* CHPL2D_G8_FAST / HPLS_G8_FAST */
+    int64_t chunk;      /* column chunk of the update (CHPL2D_G8_NT / HPLS_G8_CHUNK), 0 = auto */
+    int lookahead;      /* depth-1 lookahead on a high-priority stream (1) or serial (0) */
+    uint64_t seed;      /* 42 */
+    double threshold;   /* HPL.dat line 13 (16.0) */
+    int verbose;        /* print progress lines */
+} chpl_hpl_config;
+
+typedef struct chpl_hpl_result {
+    double time_s;      /* factor + solve, device time (matgen excluded, as HPL) */
+    double tflops;      /* (2/3 N^3 + 2 N^2) / time_s / 1e12 */
+    double resid;       /* scaled residual */
+    int passed;         /* resid < threshold */
+    double matgen_s;
+    double phase_s[8];  /* panel, laswp, trsm, update(emulated), update(fp64), backsolve, comm, other */
+    int64_t n_emulated; /* number of emulated update calls */
+} chpl_hpl_result;
+
+/* Fill cfg with the defaults of chpl_single / chpl_p2 (src/chpl_p2.cu:570-584). */
+void chpl_hpl_default_config(chpl_hpl_config *cfg);
+
+/*
+ * One HPL run on the current device (P = Q = 1): generate, factor and solve,
+ * verify.  x_out (host, N doubles) may be NULL.  Replaces run_case of
+ * chpl_single (src/chpl_single.cu:733-840).
+ */
+int chpl_hpl_run(const chpl_hpl_config *cfg, chpl_hpl_result *res, double *x_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHPL_H */

@@ -1,0 +1,150 @@
+"""GPU parity of the HPL building blocks and solves, through the C ABI."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import scipy.linalg
+import torch
+
+import oracle
+from chpl_b200 import _lib, hpl
+from gpu_util import empty_bytes, from_dev, to_dev
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_matgen_bitexact(cuda):
+    L = _lib.load()
+    N = 300
+    m, n, row0, col0 = 123, 77, 45, 200
+    d = torch.zeros((n, 130), dtype=torch.float64, device="cuda")
+    _lib.check(L.chpl_matgen(0, d.data_ptr(), 130, m, n, row0, col0, N + 1, 42), "chpl_matgen")
+    torch.cuda.synchronize()
+    got = from_dev(d, m, n)
+    ref = oracle.matgen(m, n, seed=42, row0=row0, col0=col0, ncg=N + 1)
+    assert np.array_equal(got, ref)
+
+
+def test_matgen_golden(cuda):
+    L = _lib.load()
+    d = torch.zeros((65, 64), dtype=torch.float64, device="cuda")
+    _lib.check(L.chpl_matgen(0, d.data_ptr(), 64, 64, 65, 0, 0, 65, 42), "chpl_matgen")
+    torch.cuda.synchronize()
+    assert np.array_equal(from_dev(d, 64, 65), np.load(os.path.join(GOLDEN, "matgen_N64_seed42.npz"))["A"])
+
+
+@pytest.mark.parametrize("grid", [(1, 2, 0, 1), (2, 2, 1, 0), (2, 4, 1, 3)])
+def test_matgen_cyclic(cuda, grid):
+    P, Q, pr, qc = grid
+    N, NB = 1000, 64
+    L = _lib.load()
+    S = oracle.hpl_system(N)
+    rows = [g for g in range(N) if (g // NB) % P == pr]
+    cols = [g for g in range(N + 1) if (g // NB) % Q == qc]
+    d = torch.zeros((len(cols), len(rows)), dtype=torch.float64, device="cuda")
+    _lib.check(L.chpl_matgen_cyclic(0, d.data_ptr(), len(rows), N, NB, P, Q, pr, qc, 42), "matgen_cyclic")
+    torch.cuda.synchronize()
+    assert np.array_equal(from_dev(d, len(rows), len(cols)), S[np.ix_(rows, cols)])
+
+
+@pytest.mark.parametrize("case", [(500, 64, 0), (2000, 1024, 300), (3000, 2048, 10)])
+def test_laswp_bitexact(cuda, case):
+    nrows, ns, k1 = case
+    L = _lib.load()
+    rng = np.random.default_rng(ns)
+    ncols = 37
+    A = rng.standard_normal((nrows, ncols))
+    ipiv = np.arange(nrows, dtype=np.int64)
+    for i in range(k1, k1 + ns):
+        ipiv[i] = rng.integers(i, nrows)
+    dA, lda = to_dev(A)
+    dpiv = torch.from_numpy(ipiv).cuda()
+    work = empty_bytes(L.chpl_laswp_work_bytes(nrows, ns))
+    _lib.check(L.chpl_laswp(0, dA.data_ptr(), lda, ncols, k1, k1 + ns, dpiv.data_ptr(), nrows, work.data_ptr()),
+               "chpl_laswp")
+    torch.cuda.synchronize()
+    ref = oracle.laswp(np.asfortranarray(A.copy()), ipiv, k1, k1 + ns)
+    assert np.array_equal(from_dev(dA, nrows, ncols), ref)
+
+
+@pytest.mark.parametrize("mn", [(1000, 128), (4096, 1024), (257, 64)])
+def test_panel_getrf(cuda, mn):
+    m, n = mn
+    L = _lib.load()
+    rng = np.random.default_rng(m + n)
+    A = rng.uniform(-0.5, 0.5, (m, n))
+    dA, lda = to_dev(A)
+    piv = torch.zeros(n, dtype=torch.int64, device="cuda")
+    info = torch.zeros(1, dtype=torch.int32, device="cuda")
+    work = empty_bytes(L.chpl_panel_getrf_work_bytes(m, n))
+    _lib.check(L.chpl_panel_getrf_f64(0, m, n, dA.data_ptr(), lda, piv.data_ptr(), info.data_ptr(),
+                                      work.data_ptr()), "panel_getrf")
+    torch.cuda.synchronize()
+    lu, p = scipy.linalg.lu_factor(A)
+    assert info.item() == 0
+    assert np.array_equal(piv.cpu().numpy(), p)
+    got = from_dev(dA, m, n)
+    assert np.allclose(got, lu, rtol=1e-11, atol=1e-12)
+
+
+def test_residual_matches_oracle(cuda):
+    L = _lib.load()
+    N = 700
+    S = oracle.hpl_system(N)
+    x = np.linalg.solve(S[:, :N], S[:, N]) * (1 + 1e-12)
+    dx = torch.from_numpy(x).cuda()
+    r = ctypes.c_double()
+    _lib.check(L.chpl_residual(0, N, 42, dx.data_ptr(), ctypes.byref(r)), "chpl_residual")
+    assert r.value == pytest.approx(oracle.hpl_residual(x, N), rel=1e-6)
+
+
+def test_hpl_fp64_small(cuda):
+    cfg = hpl.Config(N=1000, NB=128, emulate=False, lookahead=False)
+    res = hpl.run(cfg, want_x=True)
+    assert res.passed and res.resid < 1.0
+    S = oracle.hpl_system(1000)
+    xs = np.linalg.solve(S[:, :1000], S[:, 1000])
+    assert np.allclose(res.x, xs, rtol=1e-9, atol=1e-9)
+
+
+def test_hpl_golden_fp64(cuda):
+    fx = np.load(os.path.join(GOLDEN, "hpl_N256_NB32.npz"))
+    res = hpl.run(hpl.Config(N=256, NB=32, emulate=False), want_x=True)
+    assert res.passed
+    assert np.allclose(res.x, fx["x"], rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("L", [11, 12])
+def test_hpl_emulated_passes(cuda, L):
+    cfg = hpl.Config(N=4096, NB=256, moduli=L, lookahead=True)
+    res = hpl.run(cfg, want_x=True)
+    assert res.passed, res.resid
+    assert res.n_emulated > 0
+
+
+def test_hpl_lookahead_is_deterministic(cuda):
+    """Lookahead only reorders independent work: x is bit-identical to the
+    serial schedule, and reruns are bit-identical (src/chpl_p2.cu residuals are
+    deterministic per configuration)."""
+    a = hpl.run(hpl.Config(N=3000, NB=256, moduli=12, lookahead=True), want_x=True)
+    b = hpl.run(hpl.Config(N=3000, NB=256, moduli=12, lookahead=False), want_x=True)
+    c = hpl.run(hpl.Config(N=3000, NB=256, moduli=12, lookahead=True), want_x=True)
+    assert np.array_equal(a.x, b.x) and np.array_equal(a.x, c.x)
+    assert a.resid == b.resid == c.resid
+
+
+def test_hpl_ragged_sizes(cuda):
+    """N not a multiple of NB, chunked update with tail absorption."""
+    res = hpl.run(hpl.Config(N=2500, NB=192, moduli=12, chunk=700), want_x=True)
+    assert res.passed, res.resid
+
+
+def test_hpl_emulated_vs_oracle_small(cuda):
+    """The whole emulated solve against the CPU restatement at a small size."""
+    N, NB = 384, 64
+    res = hpl.run(hpl.Config(N=N, NB=NB, moduli=12, lookahead=False), want_x=True)
+    x, _, _ = oracle.hpl_solve(N, NB, L=12)
+    assert np.allclose(res.x, x, rtol=1e-6, atol=1e-8)
+    assert res.passed

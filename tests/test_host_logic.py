@@ -1,0 +1,73 @@
+"""CPU tests of the host-side logic: HPL.dat and environment configuration,
+block-cyclic maps, flop count, report formats."""
+import os
+
+import numpy as np
+import pytest
+
+from chpl_b200 import hpl
+
+
+def test_read_hpl_dat_fields(tmp_path):
+    p = tmp_path / "HPL.dat"
+    hpl.write_hpl_dat(str(p), 393216, 4096, 2, 4, 16.0)
+    d = hpl.read_hpl_dat(str(p))
+    assert (d.N, d.NB, d.P, d.Q, d.threshold) == (393216, 4096, 2, 4, 16.0)
+
+
+def test_read_hpl_dat_fallback(tmp_path):
+    # fewer than 13 lines or missing file: N=16384, NB=1024, 16.0 (src/chpl_p2.cu:570-584)
+    p = tmp_path / "short.dat"
+    p.write_text("a\nb\n")
+    d = hpl.read_hpl_dat(str(p))
+    assert (d.N, d.NB, d.threshold) == (16384, 1024, 16.0)
+    d = hpl.read_hpl_dat(str(tmp_path / "missing.dat"))
+    assert (d.N, d.NB) == (16384, 1024)
+
+
+def test_reference_hpl_dat_layout(tmp_path):
+    """The 13-line layout of scripts/HPL.dat (N on line 6, NB on 8, threshold on 13)."""
+    text = ("HPLinpack benchmark input file\nInnovative Computing Laboratory, University of Tennessee\n"
+            "HPL.out      output file name (if any)\n6            device out (6=stdout,7=stderr,file)\n"
+            "1            # of problems sizes (N)\n460800       Ns\n1            # of NBs\n4096         NBs\n"
+            "0            PMAP process mapping (0=Row-,1=Column-major)\n1            # of process grids (P x Q)\n"
+            "4            Ps\n4            Qs\n16.0         threshold\n")
+    p = tmp_path / "HPL.dat"
+    p.write_text(text)
+    d = hpl.read_hpl_dat(str(p))
+    assert (d.N, d.NB, d.P, d.Q, d.threshold) == (460800, 4096, 4, 4, 16.0)
+
+
+def test_single_env_config():
+    env = {"HPLS_NB": "512", "HPLS_BACKEND": "gemmul8", "HPLS_G8_MODULI": "12", "HPLS_G8_FAST": "1",
+           "HPLS_G8_CHUNK": "3072", "HPLS_SEED": "7"}
+    c = hpl.single_config_from_env(8192, env)
+    assert (c.N, c.NB, c.moduli, c.fast, c.chunk, c.seed, c.emulate) == (8192, 512, 12, True, 3072, 7, True)
+    assert hpl.single_config_from_env(2000, {"HPLS_BACKEND": "native"}).emulate is False
+    with pytest.raises(ValueError):
+        hpl.single_config_from_env(2000, {"HPLS_BACKEND": "bogus"})
+    with pytest.raises(ValueError):
+        hpl.single_config_from_env(100, {"HPLS_NB": "200"})
+
+
+def test_grid_env_config():
+    d = hpl.HplDat(N=131072, NB=2048, threshold=16.0)
+    c = hpl.grid_config_from_env(d, 2, 4, {"CHPL2D_G8": "1", "CHPL2D_G8_MODULI": "12"})
+    assert (c.N, c.NB, c.P, c.Q, c.moduli, c.emulate) == (131072, 2048, 2, 4, 12, True)
+    assert hpl.grid_config_from_env(d, 1, 2, {"CHPL2D_G8": "0"}).emulate is False
+    # launcher default (scripts/mpirun_chpl:107-126): 11 moduli, fast
+    c = hpl.grid_config_from_env(d, 1, 1, {})
+    assert (c.moduli, c.fast, c.emulate) == (11, True, True)
+
+
+def test_flop_count():
+    assert hpl.flops(1000) == pytest.approx(2.0 / 3.0 * 1e9 + 2e6)
+
+
+def test_report_formats():
+    r = hpl.Result(N=1000, NB=128, P=2, Q=4, time_s=1.5, tflops=0.5, resid=1.25, passed=True, threshold=16.0,
+                   matgen_s=0.1)
+    s = hpl.format_grid(r)
+    assert "WC2" in s and "PASSED" in s and "1000" in s
+    s = hpl.format_single(r, hpl.Config(N=1000, NB=128))
+    assert "HPLS_gemmul8" in s and "PASSED" in s

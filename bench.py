@@ -1,0 +1,276 @@
+#!/usr/bin/env python
+"""bench.py -- HPL FP64-equivalent TFLOPS on B200 (the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl chpl|reference]
+
+One step = one HPL solve (factor + back substitution) of the generated system,
+with the matrix generated in HBM before the step's timed region (HPL excludes
+generation, src/chpl_single.cu:756-757, src/chpl_p2.cu:965-966).  Workload at
+N=1: BASELINE config 3 (N=139264, NB=1024, 1x1 grid, 11 moduli, ~155 GB).
+Multi-GPU runs are weak-scaled to ~155 GB per GPU on the grids 1x2, 2x2, 2x4
+(config 4 at 8 GPUs: N=393216, NB=4096, P2Q4).
+
+One JSON line is printed by rank 0.  --impl reference times the CPU baseline
+(host FP64 LU, LAPACK dgetrf+dgetrs through OpenBLAS on all host cores) on a
+bounded sample of the same generated system.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import ctypes
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "HPL FP64-equiv TFLOPS (2/3N³+2N²)/t at 1/2/4/8 B200; scaled residual"
+# per-GPU-count workloads: (N, NB, P, Q)
+WORKLOADS = {
+    1: (139264, 1024, 1, 1),
+    2: (196608, 2048, 1, 2),
+    4: (278528, 2048, 2, 2),
+    8: (393216, 4096, 2, 4),
+}
+CPU_SAMPLE_N = 32768
+
+
+def flops(N: int) -> float:
+    return (2.0 / 3.0) * N ** 3 + 2.0 * N ** 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["chpl", "reference"], default="chpl")
+    ap.add_argument("--N", type=int, default=0, help="override the order (profiling / small runs)")
+    ap.add_argument("--NB", type=int, default=0)
+    ap.add_argument("--moduli", type=int, default=11)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-lookahead", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                self.out, _ = self.p.communicate()
+
+    def summary(self) -> dict:
+        rows = [r for r in csv.reader(io.StringIO(getattr(self, "out", "") or "")) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def f(x):
+            try:
+                return float(x.strip())
+            except ValueError:
+                return None
+        load = [r for r in rows if (f(r[3]) or 0.0) > 300.0] or rows
+        sm = [f(r[1]) for r in load if f(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": f(rows[0][2]),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": max((f(r[3]) or 0.0) for r in rows)}
+
+
+# ----------------------------------------------------------------------------- helpers
+def int8_peak_tops() -> float:
+    """cuBLAS int8 GEMM (torch._int_mm, 8192^3), best of 10: the tensor-pipe
+    denominator for the int8 kernel (MEASURED_PEAKS.json carries no int8 figure)."""
+    import torch
+    n = 8192
+    a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
+    torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 1e30
+    for _ in range(10):
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e-3)
+    del a, b
+    torch.cuda.empty_cache()
+    return 2.0 * n ** 3 / best / 1e12
+
+
+def measured_peaks() -> dict:
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def traffic_per_unit():
+    """DRAM bytes per int8 multiply-add of the GEMM kernel from the committed
+    ncu summary (profiles/oz2_gemm_kernel_c2.json), or None."""
+    p = os.path.join(ROOT, "profiles", "oz2_gemm_kernel_c2.json")
+    try:
+        d = json.load(open(p))
+        return d["dram_bytes"] / d["int8_macs"]
+    except (OSError, ValueError, KeyError):
+        return None
+
+
+def cpu_baseline(N: int) -> dict:
+    """Host FP64 LU (OpenBLAS via scipy) on the same generated system, N x (N+1)."""
+    import oracle
+    A = oracle.hpl_system_fast(N)
+    t0 = time.perf_counter()
+    x = oracle.lapack_hpl_solve(A)
+    t = time.perf_counter() - t0
+    del A
+    r = oracle.hpl_residual_from(oracle.hpl_system_fast(N), x) if N <= 40000 else None
+    return {"value": flops(N) / t / 1e12, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"HPL solve N={N} (same generator, seed 42): LAPACK dgetrf+dgetrs (OpenBLAS, "
+                      f"{os.cpu_count()} threads), generation excluded, {t:.1f} s",
+            "resid": r}
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(a) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    N = a.N or CPU_SAMPLE_N
+    times = []
+    for i in range(a.warmup + a.steps):
+        A = oracle.hpl_system_fast(N)
+        t0 = time.perf_counter()
+        oracle.lapack_hpl_solve(A)
+        t = time.perf_counter() - t0
+        if i >= a.warmup:
+            times.append(t)
+        del A
+    tot = sum(times)
+    v = a.steps * flops(N) / tot / 1e12
+    wl = WORKLOADS.get(a.gpus, WORKLOADS[1])
+    print(json.dumps({
+        "metric": METRIC, "value": v, "unit": "TFLOPS", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": tot / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp64", "data": "synthetic (chpl SplitMix64 generator, seed 42)", "impl": "reference",
+        "config": {"workload": f"HPL solve N={wl[0]} NB={wl[1]} {wl[2]}x{wl[3]} (sampled on the host at N={N})",
+                   "grid": f"{wl[2]}x{wl[3]}"},
+        "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"HPL solve N={N} per step, LAPACK dgetrf+dgetrs (OpenBLAS, "
+                                   f"{os.cpu_count()} threads); the reference itself has no CPU path"},
+        "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------------------- chpl arm
+def run_single(a) -> None:
+    import torch
+
+    from chpl_b200 import _lib, hpl
+    N, NB = (a.N, a.NB or 1024) if a.N else WORKLOADS[1][:2]
+    cfg = hpl.Config(N=N, NB=NB, moduli=a.moduli, lookahead=not a.no_lookahead)
+    torch.cuda.set_device(0)
+    peak_i8 = int8_peak_tops()
+    for _ in range(a.warmup):
+        hpl.run(cfg)
+    torch.cuda.synchronize()
+    res = []
+    walls = []
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        for _ in range(a.steps):
+            t0 = time.perf_counter()
+            r = hpl.run(cfg, want_x=True)       # public API: generate, solve, verify, x -> host
+            walls.append(time.perf_counter() - t0)
+            res.append(r)
+        torch.cuda.synchronize()
+    solve = sum(r.time_s for r in res)
+    value = a.steps * flops(N) / solve / 1e12
+    gk = sum(r.gemm_kernel_s for r in res)
+    ops = sum(r.gemm_int8_ops for r in res)
+    nl = sum(r.gemm_launches for r in res)
+    achieved = ops / gk / 1e12 if gk > 0 else None
+    tpu = traffic_per_unit()
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak_i8, "unit": "TOPS (int8)",
+            "frac": achieved / peak_i8 if achieved else None,
+            "traffic": (tpu * ops / 2.0 / nl) if (tpu and nl) else None,
+            "kernel": "oz2_gemm_kernel (tcgen05 kind::i8 + fused CRT)",
+            "peak_source": "cuBLAS int8 GEMM 8192^3 measured in this run (MEASURED_PEAKS.json has no int8 "
+                           f"figure; 2 x its bf16 burst = {2 * measured_peaks().get('bf16_tflops', 0):.0f})",
+            "launches": nl, "avg_launch_ms": gk / nl * 1e3 if nl else None,
+            "fp64eq_tflops_in_kernel": sum(r.gemm_fp64eq_flops for r in res) / gk / 1e12 if gk else None}
+    phases = {p: sum(r.phases[p] for r in res) / a.steps for p in hpl.PHASES}
+    out = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": solve / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"int8 tensor cores (Ozaki-II, {a.moduli} moduli) + fp64",
+        "data": "synthetic (chpl SplitMix64 generator, seed 42)",
+        "config": {"workload": f"HPL solve N={N} NB={NB} 1x1 grid, {a.moduli} moduli (BASELINE config 3)"
+                   if not a.N else f"HPL solve N={N} NB={NB} 1x1 grid, {a.moduli} moduli",
+                   "N": N, "NB": NB, "grid": "1x1", "moduli": a.moduli, "lookahead": not a.no_lookahead,
+                   "l2": f"inputs larger than L2 ({N * (N + 1) * 8 / 1e9:.1f} GB matrix)",
+                   "timed_region": "factor + back substitution per step (device events); generation excluded"},
+        "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
+        "phases_s": phases,
+        "roofline": roof,
+        "e2e": {"value": a.steps * flops(N) / sum(walls) / 1e12, "unit": "TFLOPS",
+                "h2d_bytes_per_step": ctypes.sizeof(_lib.HplConfig),
+                "d2h_bytes_per_step": N * 8 + ctypes.sizeof(_lib.HplResult),
+                "note": "public API chpl_hpl_run per step (wall clock): allocation, on-device generation "
+                        "(HPL defines A,b as generated), solve, verification, x to host"},
+        "gpu_launches": sum(r.n_launches for r in res),
+        "clocks": clk.summary(),
+    }
+    if not a.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(CPU_SAMPLE_N)
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+        return
+    if a.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        run_single(a)
+        return
+    from chpl_b200 import grid
+    grid.bench(a, WORKLOADS, METRIC, flops, ClockSampler)
+
+
+if __name__ == "__main__":
+    main()

@@ -50,7 +50,7 @@ namespace chpl {
         }                                                                          \
     } while (0)
 
-enum Phase { PH_PANEL = 0, PH_LASWP, PH_TRSM, PH_UPD_EMU, PH_UPD_FP64, PH_SOLVE, PH_COMM, PH_OTHER, PH_N };
+enum Phase { PH_PANEL = 0, PH_LASWP, PH_TRSM, PH_SPLIT, PH_GEMM, PH_UPD_FP64, PH_SOLVE, PH_COMM, PH_N };
 
 namespace {
 
@@ -106,6 +106,9 @@ struct Solver {
     size_t wsA = 0, wsRest = 0;
     int64_t chunk = 0;
     int64_t n_emu = 0;
+    int64_t n_launch = 0;          // kernels of this library issued in factor + solve
+    std::vector<PhaseTimer::Rec> gemm_recs;   // one per tcgen05 GEMM launch
+    double gemm_ops = 0.0, gemm_flops = 0.0;
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_next = 0;
     PhaseTimer clk;
@@ -220,6 +223,7 @@ struct Solver {
                                        fwd, fwork_h, fwh, info + 1));
         CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
         CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, lwork[k & 1]));
+        n_launch += 2;
         CHPL_TRY(clk.end(sP, r));
         return CHPL_OK;
     }
@@ -233,6 +237,7 @@ struct Solver {
         PhaseTimer::Rec r;
         CHPL_TRY(clk.begin(st, PH_LASWP, r));
         CHPL_TRY(laswp_apply(st, A, (size_t)ld, c0, nc, nb, lwork[k & 1]));
+        ++n_launch;
         CHPL_TRY(clk.end(st, r));
         CHPL_TRY(clk.begin(st, PH_TRSM, r));
         CHPL_CUBLAS(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, nb, nc,
@@ -255,18 +260,43 @@ struct Solver {
             CHPL_TRY(clk.end(st, r));
             return CHPL_OK;
         }
-        CHPL_TRY(clk.begin(st, PH_UPD_EMU, r));
+        const oz2::Moduli* M = oz2::moduli(cfg.moduli);
         for (int64_t c = 0; c < nc;) {
             int64_t w = std::min(chunk, nc - c);
             if (nc - c - w > 0 && nc - c - w < 1024) w = nc - c;  // absorb a narrow tail (src/chpl_single.cu:637-639)
-            const int skipA = (split_a && c == 0) ? 0 : 1;
-            CHPL_TRY(chpl_oz2_gemm(st, CHPL_OP_N, CHPL_OP_N, (size_t)mt, (size_t)w, (size_t)nb, &mone, at(jp + nb, jp),
-                                   (size_t)ld, at(jp, c0 + c), (size_t)ld, &one, at(jp + nb, c0 + c), (size_t)ld,
-                                   (unsigned)cfg.moduli, cfg.fast, work, wA[k & 1], nullptr, 1, 0, skipA, 0, nullptr));
+            // the body of chpl_oz2_gemm, unrolled here to time split and GEMM separately
+            const oz2::Layout y = oz2::layout((size_t)mt, (size_t)w, (size_t)nb, cfg.moduli, true, false);
+            uint8_t* pa = static_cast<uint8_t*>(wA[k & 1]);
+            uint8_t* pb = static_cast<uint8_t*>(work) + y.b_off;
+            int32_t* shA = reinterpret_cast<int32_t*>(pa + y.a_shift);
+            int8_t* resA = reinterpret_cast<int8_t*>(pa + y.a_res);
+            int32_t* shB = reinterpret_cast<int32_t*>(pb + y.b_shift);
+            int8_t* resB = reinterpret_cast<int8_t*>(pb + y.b_res);
+            void* tmp = static_cast<uint8_t*>(work) + y.tmp_off;
+            CHPL_TRY(clk.begin(st, PH_SPLIT, r));
+            if (split_a && c == 0) {
+                CHPL_TRY(oz2::split(st, false, at(jp + nb, jp), (size_t)ld, (size_t)mt, (size_t)nb, cfg.moduli, M->alpha,
+                                    resA, y.mPad, y.kPad, shA, tmp));
+                n_launch += 4;
+            }
+            CHPL_TRY(oz2::split(st, true, at(jp, c0 + c), (size_t)ld, (size_t)w, (size_t)nb, cfg.moduli, M->beta, resB,
+                                y.nPad, y.kPad, shB, tmp));
+            ++n_launch;
+            CHPL_TRY(clk.end(st, r));
+            PhaseTimer::Rec g;
+            CHPL_TRY(clk.begin(st, PH_GEMM, g));
+            CHPL_TRY(oz2::gemm_launch(st, 0, (size_t)mt, (size_t)w, y.kPad, cfg.moduli, resA, y.mPad, resB, y.nPad, shA,
+                                      shB, mone, one, at(jp + nb, c0 + c), (size_t)ld, nullptr, 0,
+                                      reinterpret_cast<int8_t*>(static_cast<uint8_t*>(work) + y.scratch_off),
+                                      y.grid_max));
+            CHPL_TRY(clk.end(st, g));
+            gemm_recs.push_back(g);
+            ++n_launch;
+            gemm_ops += 2.0 * (double)mt * (double)w * (double)y.kPad * cfg.moduli;
+            gemm_flops += 2.0 * (double)mt * (double)w * (double)nb;
             ++n_emu;
             c += w;
         }
-        CHPL_TRY(clk.end(st, r));
         return CHPL_OK;
     }
 
@@ -315,6 +345,20 @@ struct Solver {
         CHPL_TRY(clk.end(s0, r));
         return CHPL_OK;
     }
+
+    void gemm_stats(chpl_hpl_result* res)
+    {
+        double t = 0.0;
+        for (auto& g : gemm_recs) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, g.a, g.b) == cudaSuccess) t += ms * 1e-3;
+        }
+        res->gemm_launches = (int64_t)gemm_recs.size();
+        res->gemm_kernel_s = t;
+        res->gemm_int8_ops = gemm_ops;
+        res->gemm_fp64eq_flops = gemm_flops;
+        res->n_launches = n_launch;
+    }
 };
 
 }  // namespace
@@ -358,6 +402,7 @@ int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_o
     res->tflops = ((2.0 / 3.0) * dN * dN * dN + 2.0 * dN * dN) / res->time_s / 1e12;
     s.clk.sums(res->phase_s);
     res->n_emulated = s.n_emu;
+    s.gemm_stats(res);
     // x = column N
     double* dx = s.at(0, s.N);
     rc = residual(s.s0, s.N, cfg->seed, dx, &res->resid);

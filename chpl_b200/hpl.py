@@ -137,10 +137,15 @@ class Result:
     matgen_s: float
     phases: dict = field(default_factory=dict)
     n_emulated: int = 0
+    n_launches: int = 0
+    gemm_launches: int = 0
+    gemm_kernel_s: float = 0.0
+    gemm_int8_ops: float = 0.0
+    gemm_fp64eq_flops: float = 0.0
     x: np.ndarray | None = None
 
 
-PHASES = ["panel", "laswp", "trsm", "update_emulated", "update_fp64", "back_solve", "comm", "other"]
+PHASES = ["panel", "laswp", "trsm", "oz2_split", "oz2_gemm", "update_fp64", "back_solve", "comm"]
 
 
 def flops(N: int) -> float:
@@ -158,7 +163,9 @@ def run(cfg: Config, want_x: bool = False) -> Result:
     _lib.check(L.chpl_hpl_run(ctypes.byref(c), ctypes.byref(r), xp), "chpl_hpl_run")
     return Result(N=cfg.N, NB=cfg.NB, P=cfg.P, Q=cfg.Q, time_s=r.time_s, tflops=r.tflops, resid=r.resid,
                   passed=bool(r.passed), threshold=cfg.threshold, matgen_s=r.matgen_s,
-                  phases={p: r.phase_s[i] for i, p in enumerate(PHASES)}, n_emulated=r.n_emulated, x=x)
+                  phases={p: r.phase_s[i] for i, p in enumerate(PHASES)}, n_emulated=r.n_emulated,
+                  n_launches=r.n_launches, gemm_launches=r.gemm_launches, gemm_kernel_s=r.gemm_kernel_s,
+                  gemm_int8_ops=r.gemm_int8_ops, gemm_fp64eq_flops=r.gemm_fp64eq_flops, x=x)
 
 
 def format_single(res: Result, cfg: Config) -> str:

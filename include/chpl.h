@@ -184,8 +184,14 @@ typedef struct chpl_hpl_result {
     double resid;       /* scaled residual */
     int passed;         /* resid < threshold */
     double matgen_s;
-    double phase_s[8];  /* panel, laswp, trsm, update(emulated), update(fp64), backsolve, comm, other */
-    int64_t n_emulated; /* number of emulated update calls */
+    double phase_s[8];  /* per-stream busy time: panel, laswp, trsm, oz2 split, oz2 int8 GEMM + CRT,
+                           FP64 update, back solve, communication */
+    int64_t n_emulated; /* emulated update calls */
+    int64_t n_launches; /* kernels of this library launched inside factor + solve */
+    int64_t gemm_launches;      /* launches of the tcgen05 int8 GEMM kernel */
+    double gemm_kernel_s;       /* their summed device time (CUDA events on their streams) */
+    double gemm_int8_ops;       /* 2 * m * n * kPad * moduli summed over those launches */
+    double gemm_fp64eq_flops;   /* 2 * m * n * k summed over those launches */
 } chpl_hpl_result;
 
 /* Fill cfg with the defaults of chpl_single / chpl_p2 (src/chpl_p2.cu:570-584). */

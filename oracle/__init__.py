@@ -230,3 +230,32 @@ def hpl_residual_from(A: np.ndarray, x: np.ndarray) -> float:
     return float(np.max(np.abs(Ax - b)) /
                  (eps * (np.max(np.sum(np.abs(A[:, :N]), axis=1)) * np.max(np.abs(x))
                          + np.max(np.abs(b))) * N))
+
+
+def hpl_system_fast(N: int, seed: int = 42, threads: int | None = None) -> np.ndarray:
+    """The N x (N+1) system, generated by the C oracle in parallel column slabs."""
+    import concurrent.futures as cf
+    threads = threads or os.cpu_count() or 1
+    A = np.empty((N, N + 1), dtype=np.float64, order="F")
+    nc = N + 1
+    step = (nc + threads - 1) // threads
+    L = lib()
+
+    def work(c0):
+        c1 = min(nc, c0 + step)
+        if c1 > c0:
+            L.orc_matgen(ctypes.c_void_p(A.ctypes.data + c0 * N * 8), N, N, c1 - c0, 0, c0, nc, seed)
+
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(work, range(0, nc, step)))
+    return A
+
+
+def lapack_hpl_solve(A: np.ndarray):
+    """Host FP64 blocked LU with partial pivoting (LAPACK dgetrf + dgetrs via
+    scipy/OpenBLAS) of the N x (N+1) system; the CPU baseline of the hot path.
+    Returns x.  The factorization overwrites A."""
+    import scipy.linalg
+    N = A.shape[0]
+    lu, piv = scipy.linalg.lu_factor(A[:, :N], overwrite_a=True, check_finite=False)
+    return scipy.linalg.lu_solve((lu, piv), A[:, N], check_finite=False)

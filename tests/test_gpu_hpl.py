@@ -93,11 +93,12 @@ def test_residual_matches_oracle(cuda):
     L = _lib.load()
     N = 700
     S = oracle.hpl_system(N)
-    x = np.linalg.solve(S[:, :N], S[:, N]) * (1 + 1e-12)
+    x = np.linalg.solve(S[:, :N], S[:, N]) * (1 + 1e-6)   # residual dominated by the perturbation
     dx = torch.from_numpy(x).cuda()
     r = ctypes.c_double()
     _lib.check(L.chpl_residual(0, N, 42, dx.data_ptr(), ctypes.byref(r)), "chpl_residual")
-    assert r.value == pytest.approx(oracle.hpl_residual(x, N), rel=1e-6)
+    assert r.value == pytest.approx(oracle.hpl_residual(x, N), rel=1e-3)
+    assert r.value > 16.0
 
 
 def test_hpl_fp64_small(cuda):

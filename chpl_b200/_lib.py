@@ -55,6 +55,8 @@ SIGNATURES = {
                                  ctypes.POINTER(_sz)]),
     "chpl_oz2_gemm": (_int, [_vp, _int, _int, _sz, _sz, _sz, _dp, _vp, _sz, _vp, _sz, _dp, _vp, _sz, _uint, _int,
                              _vp, _vp, _vp, _int, _int, _int, _int, _dp]),
+    "chpl_oz2_gemm_noalloc": (_int, [_vp, _int, _int, _sz, _sz, _sz, _dp, _vp, _sz, _vp, _sz, _dp, _vp, _sz,
+                                     _uint]),
     "chpl_oz2_split_rows": (_int, [_vp, _int, _sz, _sz, _vp, _sz, _uint, _vp, _sz, _sz, _vp, _vp]),
     "chpl_oz2_split_cols": (_int, [_vp, _int, _sz, _sz, _vp, _sz, _uint, _vp, _sz, _sz, _vp, _vp]),
     "chpl_oz2_split_tmp_bytes": (_sz, [_sz]),

@@ -26,7 +26,7 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
                   "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
-LIB_SOURCES = ["capi.cu", "oz2.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu", "hpl_grid.cu"]
+LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu", "hpl_grid.cu"]
 LINK = ["-cudart", "shared", "-lcublas", "-lcusolver", "-lnccl",
         "-Xlinker", "-rpath," + os.path.join(CUDA, "lib64")]
 EXES = {"chpl_single": "chpl_single_main.cpp", "chpl_p2": "chpl_p2_main.cpp"}

@@ -562,7 +562,7 @@ int num_sms()
     return n;
 }
 
-Layout layout(size_t m, size_t n, size_t k, int L, bool extA, bool extB)
+Layout layout(size_t m, size_t n, size_t k, int L, bool extA, bool extB, int grid_cap)
 {
     Layout y;
     y.mPad = round_up(m, BM);
@@ -578,6 +578,7 @@ Layout layout(size_t m, size_t n, size_t k, int L, bool extA, bool extB)
     y.a_off = off; if (!extA) off += y.a_bytes;
     y.b_off = off; if (!extB) off += y.b_bytes;
     y.grid_max = num_sms();
+    if (grid_cap > 0 && grid_cap < y.grid_max) y.grid_max = grid_cap;
     y.scratch_off = off;
     off += round_up((size_t)y.grid_max * L * SCRATCH_TILE, 256);
     y.tmp_off = off;

@@ -36,7 +36,8 @@ struct Layout {
 
 const Moduli* moduli(int L);
 int num_sms();
-Layout layout(size_t m, size_t n, size_t k, int L, bool extA, bool extB);
+// grid_cap > 0 limits the persistent GEMM grid (and so the CRT scratch) to grid_cap CTAs
+Layout layout(size_t m, size_t n, size_t k, int L, bool extA, bool extB, int grid_cap = 0);
 size_t split_tmp_bytes(size_t nvec);
 int split(cudaStream_t st, bool contiguous, const double* x, size_t ld, size_t nvec, size_t k, unsigned L, int bits,
           int8_t* res, size_t ldvec, size_t ldk, int32_t* shift, void* tmp);

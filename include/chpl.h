@@ -110,6 +110,27 @@ int chpl_oz2_split_cols(void *stream, int opB, size_t k, size_t n, const double 
 size_t chpl_oz2_split_tmp_bytes(size_t num_vectors);
 int chpl_oz2_products(void *stream, size_t m, size_t n, size_t k, unsigned num_moduli, const int8_t *ra,
                       size_t lda_vec, const int8_t *rb, size_t ldb_vec, size_t ld_k, int32_t *P, size_t ldp);
+/*
+ * Allocation-free emulated GEMM.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory when they need the update --
+ * hosts whose framework reserves the whole device memory pool up front, and
+ * latency-sensitive callers that cannot take the synchronization a
+ * cudaMalloc / cudaFree may imply.  Same operation and results as
+ * chpl_oz2_gemm (fast mode, no skip flags, no phase times), with no `work`
+ * argument: all scratch lives in a fixed 64 MiB device array inside libchpl,
+ * which every GPU that loads the library keeps until process exit.  Sizes
+ * whose scratch exceeds 64 MiB are rejected with CHPL_ERR_WORKSPACE (the
+ * scratch is about L*(m_pad + n_pad)*k_pad bytes plus 2 MiB per modulus, with
+ * m_pad, k_pad rounded up to 128 and n_pad to 256; e.g. m = n = k = 1024 at 12
+ * moduli fits).  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  All calls on a device share the array and
+ * it keeps the last call's contents, so calls that overlap on the GPU (other
+ * streams, other host threads) race: serialize them.  Nothing is allocated.
+ */
+int chpl_oz2_gemm_noalloc(void *stream, int opA, int opB, size_t m, size_t n, size_t k, const double *alpha,
+                          const double *A, size_t lda, const double *B, size_t ldb, const double *beta,
+                          double *C, size_t ldc, unsigned num_moduli);
 /* scaling exponents (alpha, beta) used for num_moduli (host-only query) */
 int chpl_oz2_shift_bits(unsigned num_moduli, size_t k, int *alpha_bits, int *beta_bits);
 

@@ -1,0 +1,70 @@
+"""Single-case runner for timing and profiling (ncu) of the library's kernels.
+
+    python -m chpl_b200.cases gemm --m 32768 --n 32768 --k 4096 --moduli 11 [--reps 3]
+    python -m chpl_b200.cases hpl --N 65536 --NB 1024 [--no-lookahead]
+
+Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (BASELINE
+config 2) generated on the device.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import hpl, oz2
+
+
+def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool) -> dict:
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42)
+    A = torch.rand(k, m, dtype=torch.float64, device="cuda", generator=g) - 0.5   # column-major m x k
+    if scaled:
+        u = torch.randint(-20, 21, (m,), device="cuda", generator=g).double()
+        A *= torch.exp2(u)[None, :]
+    B = torch.rand(n, k, dtype=torch.float64, device="cuda", generator=g) - 0.5   # column-major k x n
+    C = torch.rand(n, m, dtype=torch.float64, device="cuda", generator=g) - 0.5   # column-major m x n
+    tot, _, _ = oz2.workSize(m, n, k, L)
+    work = torch.empty(tot, dtype=torch.uint8, device="cuda")
+    best = None
+    for _ in range(reps):
+        ph = oz2.gemm(oz2.OP_N, oz2.OP_N, m, n, k, -1.0, A, m, B, k, 1.0, C, m, L, True, work, timed=True)
+        if best is None or ph[0] + ph[1] < best[0] + best[1]:
+            best = ph
+    t = best[0] + best[1]
+    return {"case": "gemm", "m": m, "n": n, "k": k, "moduli": L, "split_ms": best[0] * 1e3, "gemm_ms": best[1] * 1e3,
+            "fp64eq_tflops": 2.0 * m * n * k / t / 1e12,
+            "kernel_int8_tops": 2.0 * m * n * (-(-k // 128) * 128) * L / best[1] / 1e12}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=32768)
+    g.add_argument("--n", type=int, default=32768)
+    g.add_argument("--k", type=int, default=4096)
+    g.add_argument("--moduli", type=int, default=11)
+    g.add_argument("--reps", type=int, default=3)
+    g.add_argument("--scaled", action="store_true")
+    h = sub.add_parser("hpl")
+    h.add_argument("--N", type=int, default=16384)
+    h.add_argument("--NB", type=int, default=1024)
+    h.add_argument("--moduli", type=int, default=11)
+    h.add_argument("--no-lookahead", action="store_true")
+    h.add_argument("--fp64", action="store_true")
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    if a.what == "gemm":
+        print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled)), flush=True)
+    else:
+        r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=not a.no_lookahead, emulate=not a.fp64))
+        print(json.dumps({"case": "hpl", "N": a.N, "NB": a.NB, "tflops": r.tflops, "time_s": r.time_s,
+                          "resid": r.resid, "passed": r.passed, "phases": r.phases,
+                          "gemm_int8_tops": r.gemm_int8_ops / r.gemm_kernel_s / 1e12 if r.gemm_kernel_s else None,
+                          "gemm_launches": r.gemm_launches}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -432,6 +432,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t buf = acc & 1u, aph = (acc >> 1) & 1u;
                 if (!mbar_wait(&acc_full[buf], aph, abort_flag)) { ok = false; break; }
                 tc_fence_after();
+                if (p.mode == 0 && l == (L >= 2 ? L - 2 : 0) && gi < p.m) {
+                    // warm L2 with this thread's C row segment (128 columns) for the final pass
+                    const int gj0 = nt * BN + half * 128;
+                    const double* cp = p.C + gi + (size_t)gj0 * p.ldc;
+                    for (int j = 0; j < 128 && gj0 + j < p.n; ++j)
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(cp + (size_t)j * p.ldc));
+                }
                 const int mod = p.M.mod[l], hi = p.M.hi[l];
                 const float inv = p.M.inv_f[l];
 #pragma unroll 1
@@ -439,6 +446,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * BN + half * 128 + c * 32, v);
                     tmem_wait_ld();
+                    if (c == 3) {  // every column of this warp is in registers: release the accumulator early
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                    }
                     if (p.mode == 1) {
                         const int gj0 = nt * BN + half * 128 + c * 32;
                         if (gi < p.m) {
@@ -462,44 +474,55 @@ __global__ void __launch_bounds__(THREADS, 1)
                         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 ++acc;
             }
             if (!ok || p.mode != 0) continue;
             // ---- CRT + unscale + C update for this warp's 32 rows x 128 columns ----
+            // 16 columns per block.  Every load of a block (16 C values, L
+            // residue words) is issued before any arithmetic, so the HBM and
+            // L2 latencies of a block overlap instead of adding up.
             if (gi < p.m) {
                 const int sa = p.shiftA[gi];
+                const bool readc = p.beta != 0.0;
+                const uint8_t* srow = reinterpret_cast<const uint8_t*>(scr) + ((size_t)(half * 4) * BM + row) * 32;
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c)
-#pragma unroll 1
-                    for (int hh = 0; hh < 2; ++hh) {
-                        unsigned long long S[16];
+                for (int blk = 0; blk < 8; ++blk) {
+                    const int c = blk >> 1, hh = blk & 1;
+                    const int gj0 = nt * BN + half * 128 + c * 32 + hh * 16;
+                    double* __restrict__ cbase = p.C + gi + (size_t)gj0 * p.ldc;
+                    double cv[16];
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) S[t] = 0ull;
-                        for (int l = 0; l < L; ++l) {
-                            const uint4 w =
-                                *reinterpret_cast<const uint4*>(scr + (((size_t)l * 8 + half * 4 + c) * BM + row) * 32 + hh * 16);
+                    for (int t = 0; t < 16; ++t)
+                        cv[t] = (readc && gj0 + t < p.n) ? __ldcs(cbase + (size_t)t * p.ldc) : 0.0;
+                    uint4 w[kMaxModuli];
+                    const uint8_t* sp = srow + (size_t)c * BM * 32 + hh * 16;
+#pragma unroll
+                    for (int l = 0; l < kMaxModuli; ++l)
+                        if (l < L) w[l] = __ldcg(reinterpret_cast<const uint4*>(sp + (size_t)l * 8 * BM * 32));
+                    unsigned long long S[16];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) S[t] = 0ull;
+#pragma unroll
+                    for (int l = 0; l < kMaxModuli; ++l) {
+                        if (l < L) {
                             const unsigned long long vl = p.M.v[l];
-                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                            const uint32_t ws[4] = {w[l].x, w[l].y, w[l].z, w[l].w};
 #pragma unroll
                             for (int t = 0; t < 16; ++t) {
                                 const int r = (int)(int8_t)((ws[t >> 2] >> (8 * (t & 3))) & 0xffu);
                                 S[t] += (unsigned long long)(long long)r * vl;
                             }
                         }
-                        const int gj0 = nt * BN + half * 128 + c * 32 + hh * 16;
+                    }
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) {
-                            const int gj = gj0 + t;
-                            if (gj < p.n) {
-                                const double prod = scalbn((double)(long long)S[t] * p.M.Mf, -(sa + __ldg(&p.shiftB[gj])));
-                                double* cp = p.C + gi + (size_t)gj * p.ldc;
-                                *cp = (p.beta == 0.0) ? p.alpha * prod : fma(p.alpha, prod, p.beta * *cp);
-                            }
+                    for (int t = 0; t < 16; ++t) {
+                        const int gj = gj0 + t;
+                        if (gj < p.n) {
+                            const double prod = scalbn((double)(long long)S[t] * p.M.Mf, -(sa + __ldg(&p.shiftB[gj])));
+                            __stcs(cbase + (size_t)t * p.ldc, readc ? fma(p.alpha, prod, p.beta * cv[t]) : p.alpha * prod);
                         }
                     }
+                }
             }
         }
     }

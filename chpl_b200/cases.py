@@ -54,13 +54,18 @@ def main() -> None:
     h.add_argument("--moduli", type=int, default=11)
     h.add_argument("--no-lookahead", action="store_true")
     h.add_argument("--fp64", action="store_true")
+    h.add_argument("--agg", type=int, default=0)
+    h.add_argument("--trsm-mode", type=int, default=0)
+    h.add_argument("--reserve", type=int, default=-1)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.what == "gemm":
         print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled)), flush=True)
     else:
-        r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=not a.no_lookahead, emulate=not a.fp64))
-        print(json.dumps({"case": "hpl", "N": a.N, "NB": a.NB, "tflops": r.tflops, "time_s": r.time_s,
+        r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=not a.no_lookahead, emulate=not a.fp64,
+                               agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve))
+        print(json.dumps({"case": "hpl", "N": a.N, "NB": a.NB, "agg": a.agg, "trsm_mode": a.trsm_mode,
+                          "lookahead": not a.no_lookahead, "tflops": r.tflops, "time_s": r.time_s,
                           "resid": r.resid, "passed": r.passed, "phases": r.phases,
                           "gemm_int8_tops": r.gemm_int8_ops / r.gemm_kernel_s / 1e12 if r.gemm_kernel_s else None,
                           "gemm_launches": r.gemm_launches}), flush=True)

@@ -24,6 +24,7 @@ size_t laswp_work_bytes(int64_t nswaps);
 int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work);
 int laswp_apply(cudaStream_t st, double* A, size_t lda, int64_t c0, int64_t ncols, int64_t nswaps, const void* work);
 int ipiv_to_abs(cudaStream_t st, const int64_t* rel, int64_t n, int64_t base, int64_t* out);
+int identity(cudaStream_t st, double* X, int64_t n);
 int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid);
 int hpl_read_clear_status(int* st);
 

@@ -214,6 +214,21 @@ int ipiv_to_abs(cudaStream_t st, const int64_t* rel, int64_t n, int64_t base, in
     return CHPL_OK;
 }
 
+__global__ void identity_kernel(double* __restrict__ X, long long n)
+{
+    const long long total = n * n;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x)
+        X[e] = (e % n == e / n) ? 1.0 : 0.0;
+}
+
+int identity(cudaStream_t st, double* X, int64_t n)
+{
+    if (n <= 0) return CHPL_OK;
+    identity_kernel<<<grid_for(n * n, 256), 256, 0, st>>>(X, (long long)n);
+    CHPL_CUDA(cudaGetLastError());
+    return CHPL_OK;
+}
+
 // ----------------------------------------------------------------------------
 // residual: regenerate A and b on the fly, deterministic two-stage reduction
 // ----------------------------------------------------------------------------

@@ -87,8 +87,9 @@ struct PhaseTimer {
 
 struct Solver {
     chpl_hpl_config cfg{};
-    int64_t N = 0, NB = 0, ld = 0, ncols = 0;
-    cudaStream_t s0 = nullptr, sP = nullptr;  // bulk update (low priority), panel chain (high priority)
+    int64_t N = 0, NB = 0, K = 0, ld = 0, ncols = 0;
+    int agg = 1, nsm = 148, reserve = 0;
+    cudaStream_t s0 = nullptr, sP = nullptr;  // bulk update (low priority), super-block chain (high priority)
     cublasHandle_t hb0 = nullptr, hbP = nullptr;
     cusolverDnHandle_t hs = nullptr;
     cusolverDnParams_t hp = nullptr;
@@ -99,15 +100,18 @@ struct Solver {
     void* fwork_d = nullptr;
     void* fwork_h = nullptr;
     size_t fwd = 0, fwh = 0;
-    void* lwork[2] = {nullptr, nullptr};   // laswp plans, by panel parity
-    void* wA[2] = {nullptr, nullptr};      // L21 residues, by panel parity (shared by both streams)
+    std::vector<void*> lw[2];              // laswp plans of the panels of a super-block, by super-block parity
+    void* wA[2] = {nullptr, nullptr};      // residues of a super-block's L21 (k = K), by parity, shared by streams
+    void* wAin = nullptr;                  // residues of a panel's L21 for the inner updates (k = NB), sP only
+    double* Linv[2] = {nullptr, nullptr};  // inv(L) of a super-block's unit lower triangle (K x K), by parity
+    void* wLinv[2] = {nullptr, nullptr};   // residues of inv(L) (A part, k = K), by parity
+    bool emu_trsm = false;                 // U12 = inv(L) * A12 through the emulated GEMM
     void* w0 = nullptr;                    // oz2 B part + scratch for s0
     void* wP = nullptr;                    // oz2 B part + scratch for sP
-    size_t wsA = 0, wsRest = 0;
     int64_t chunk = 0;
     int64_t n_emu = 0;
-    int64_t n_launch = 0;          // kernels of this library issued in factor + solve
-    std::vector<PhaseTimer::Rec> gemm_recs;   // one per tcgen05 GEMM launch
+    int64_t n_launch = 0;                  // kernels of this library issued in factor + solve
+    std::vector<PhaseTimer::Rec> gemm_recs;
     double gemm_ops = 0.0, gemm_flops = 0.0;
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_next = 0;
@@ -129,9 +133,15 @@ struct Solver {
     {
         cfg = c;
         N = c.N;
-        NB = c.NB;
+        NB = std::min<int64_t>(c.NB, N);
+        agg = c.agg > 0 ? c.agg : (int)std::max<int64_t>(1, 4096 / NB);
+        K = std::min<int64_t>(agg * NB, N);
         ld = (int64_t)round_up((size_t)N, 32);
         ncols = N + 1;
+        nsm = oz2::num_sms();
+        reserve = cfg.lookahead ? (c.reserve_sms >= 0 ? c.reserve_sms : 16) : 0;
+        reserve = std::min(reserve, nsm / 2);
+        emu_trsm = cfg.emulate && (cfg.trsm_mode == 1 || (cfg.trsm_mode == 0 && K > NB));
         int lo = 0, hi = 0;
         CHPL_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
         CHPL_CUDA(cudaStreamCreateWithPriority(&s0, cudaStreamNonBlocking, lo));
@@ -148,29 +158,34 @@ struct Solver {
         CHPL_CUSOLVER(cusolverDnCreateParams(&hp));
 
         const size_t bytesA = (size_t)ld * (size_t)ncols * sizeof(double);
-        const int64_t mmax = N > NB ? N - NB : 0;
-        const int64_t wide = ncols - NB;
-        chunk = cfg.chunk > 0 ? std::min<int64_t>(cfg.chunk, wide) : wide;
-        size_t total = 0, wsB = 0;
-        if (cfg.emulate && mmax > 0 && wide > 0) {
-            const int64_t nmax = std::min<int64_t>(chunk + 1024, wide);
-            CHPL_TRY(chpl_oz2_worksize((size_t)mmax, (size_t)nmax, (size_t)NB, (unsigned)cfg.moduli, 1, 0, &total, &wsA,
-                                       &wsB));
-            wsRest = total - wsA;
+        const int64_t mmax = std::max<int64_t>(N - NB, 0);
+        const int64_t wide = std::max<int64_t>(ncols - K, 1);
+        chunk = cfg.chunk > 0 ? std::min<int64_t>(cfg.chunk, wide) : std::min<int64_t>(32768, wide);
+        size_t tot = 0, a_big = 0, b_big = 0, tot_in = 0, a_in = 0, b_in = 0;
+        if (cfg.emulate && mmax > 0) {
+            const unsigned L = (unsigned)cfg.moduli;
+            CHPL_TRY(chpl_oz2_worksize((size_t)mmax, (size_t)std::min<int64_t>(chunk + 1024, wide), (size_t)K, L, 1, 0,
+                                       &tot, &a_big, &b_big));
+            CHPL_TRY(chpl_oz2_worksize((size_t)mmax, (size_t)std::max<int64_t>(K, 256), (size_t)NB, L, 1, 0, &tot_in,
+                                       &a_in, &b_in));
         }
+        const size_t rest0 = tot - a_big;                         // B part + scratch for s0 (k = K)
+        const size_t restP = std::max(rest0, tot_in - a_in);      // sP runs both k = K and k = NB updates
         size_t freeB = 0, totB = 0;
         CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
         CHPL_CUSOLVER(cusolverDnXgetrf_bufferSize(hs, hp, N, NB, CUDA_R_64F, nullptr, ld, CUDA_R_64F, &fwd, &fwh));
-        const int nrest = cfg.lookahead ? 2 : 1;
-        const size_t ozbytes = 2 * wsA + nrest * wsRest;
-        const size_t need = bytesA + ozbytes + fwd + 2 * laswp_work_bytes(NB) + (size_t)(2 * N + 64) * 8 +
-                            ((size_t)512 << 20);
+        const int npl = (int)((K + NB - 1) / NB);
+        const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0);
+        const size_t need = bytesA + ozbytes + fwd + 2 * npl * laswp_work_bytes(NB) + (size_t)(2 * N + 64) * 8 +
+                            ((size_t)768 << 20);
         if (cfg.verbose)
-            std::printf("MEM PLAN: matrix %.2f GiB | oz2 work %.2f GiB | getrf %.3f GiB | total %.2f GiB vs free %.2f GiB\n",
+            std::printf("MEM PLAN: matrix %.2f GiB | oz2 work %.2f GiB | getrf %.3f GiB | total %.2f GiB vs free %.2f GiB"
+                        " | K=%" PRId64 " (agg %d) reserve %d SMs\n",
                         bytesA / 1073741824.0, ozbytes / 1073741824.0, fwd / 1073741824.0, need / 1073741824.0,
-                        freeB / 1073741824.0);
+                        freeB / 1073741824.0, K, agg, reserve);
         if (need > freeB) {
-            set_error("memory plan: need %.2f GiB, %.2f GiB free (reduce N)", need / 1073741824.0, freeB / 1073741824.0);
+            set_error("memory plan: need %.2f GiB, %.2f GiB free (reduce N or HPLS_AGG)", need / 1073741824.0,
+                      freeB / 1073741824.0);
             return CHPL_ERR_WORKSPACE;
         }
         CHPL_CUDA(cudaMalloc((void**)&A, bytesA));
@@ -180,11 +195,23 @@ struct Solver {
         CHPL_CUDA(cudaMemset(info, 0, 64 * sizeof(int)));
         CHPL_CUDA(cudaMalloc(&fwork_d, fwd ? fwd : 8));
         fwork_h = std::malloc(fwh ? fwh : 8);
-        for (int b = 0; b < 2; ++b) CHPL_CUDA(cudaMalloc(&lwork[b], laswp_work_bytes(NB)));
-        if (wsA) {
-            for (int b = 0; b < 2; ++b) CHPL_CUDA(cudaMalloc(&wA[b], wsA));
-            CHPL_CUDA(cudaMalloc(&w0, wsRest));
-            if (cfg.lookahead) CHPL_CUDA(cudaMalloc(&wP, wsRest));
+        for (int b = 0; b < 2; ++b) {
+            lw[b].assign(npl, nullptr);
+            for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw[b][p], laswp_work_bytes(NB)));
+        }
+        if (a_big) {
+            for (int b = 0; b < 2; ++b) CHPL_CUDA(cudaMalloc(&wA[b], a_big));
+            CHPL_CUDA(cudaMalloc(&wAin, a_in));
+            if (emu_trsm) {
+                size_t tl = 0, al = 0;
+                CHPL_TRY(chpl_oz2_worksize((size_t)K, 256, (size_t)K, (unsigned)cfg.moduli, 1, 0, &tl, &al, nullptr));
+                for (int b = 0; b < 2; ++b) {
+                    CHPL_CUDA(cudaMalloc((void**)&Linv[b], (size_t)K * K * sizeof(double)));
+                    CHPL_CUDA(cudaMalloc(&wLinv[b], al));
+                }
+            }
+            CHPL_CUDA(cudaMalloc(&w0, cfg.lookahead ? rest0 : std::max(rest0, restP)));
+            if (cfg.lookahead) CHPL_CUDA(cudaMalloc(&wP, restP));
             else wP = w0;
         }
         return CHPL_OK;
@@ -195,9 +222,14 @@ struct Solver {
         for (auto e : ev_pool) cudaEventDestroy(e);
         if (wP && wP != w0) cudaFree(wP);
         if (w0) cudaFree(w0);
+        if (wAin) cudaFree(wAin);
+        for (int b = 0; b < 2; ++b) {
+            if (Linv[b]) cudaFree(Linv[b]);
+            if (wLinv[b]) cudaFree(wLinv[b]);
+        }
         for (int b = 0; b < 2; ++b) {
             if (wA[b]) cudaFree(wA[b]);
-            if (lwork[b]) cudaFree(lwork[b]);
+            for (void* p : lw[b]) if (p) cudaFree(p);
         }
         if (fwork_d) cudaFree(fwork_d);
         std::free(fwork_h);
@@ -213,93 +245,6 @@ struct Solver {
         if (s0) cudaStreamDestroy(s0);
     }
 
-    // factor panel k (rows jp..N-1, columns [jp, jp+nb)) on sP and plan its interchanges
-    int panel(int64_t k)
-    {
-        const int64_t jp = k * NB, nb = std::min(NB, N - jp);
-        PhaseTimer::Rec r;
-        CHPL_TRY(clk.begin(sP, PH_PANEL, r));
-        CHPL_CUSOLVER(cusolverDnXgetrf(hs, hp, N - jp, nb, CUDA_R_64F, at(jp, jp), ld, ipiv_rel, CUDA_R_64F, fwork_d,
-                                       fwd, fwork_h, fwh, info + 1));
-        CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
-        CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, lwork[k & 1]));
-        n_launch += 2;
-        CHPL_TRY(clk.end(sP, r));
-        return CHPL_OK;
-    }
-
-    // interchanges + U12 = L11^-1 A12 for columns [c0, c0+nc) of step k
-    int swap_trsm(cudaStream_t st, cublasHandle_t hb, int64_t k, int64_t c0, int64_t nc)
-    {
-        if (nc <= 0) return CHPL_OK;
-        const int64_t jp = k * NB, nb = std::min(NB, N - jp);
-        const double one = 1.0;
-        PhaseTimer::Rec r;
-        CHPL_TRY(clk.begin(st, PH_LASWP, r));
-        CHPL_TRY(laswp_apply(st, A, (size_t)ld, c0, nc, nb, lwork[k & 1]));
-        ++n_launch;
-        CHPL_TRY(clk.end(st, r));
-        CHPL_TRY(clk.begin(st, PH_TRSM, r));
-        CHPL_CUBLAS(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, nb, nc,
-                                   &one, at(jp, jp), ld, at(jp, c0), ld));
-        CHPL_TRY(clk.end(st, r));
-        return CHPL_OK;
-    }
-
-    // A22[:, c0:c0+nc] -= L21 U12 for step k; split_a: quantize L21 here
-    int gemm(cudaStream_t st, cublasHandle_t hb, void* work, int64_t k, int64_t c0, int64_t nc, bool split_a)
-    {
-        const int64_t jp = k * NB, nb = std::min(NB, N - jp), mt = N - (jp + nb);
-        if (nc <= 0 || mt <= 0) return CHPL_OK;
-        const double one = 1.0, mone = -1.0;
-        PhaseTimer::Rec r;
-        if (!cfg.emulate) {
-            CHPL_TRY(clk.begin(st, PH_UPD_FP64, r));
-            CHPL_CUBLAS(cublasDgemm_64(hb, CUBLAS_OP_N, CUBLAS_OP_N, mt, nc, nb, &mone, at(jp + nb, jp), ld, at(jp, c0),
-                                       ld, &one, at(jp + nb, c0), ld));
-            CHPL_TRY(clk.end(st, r));
-            return CHPL_OK;
-        }
-        const oz2::Moduli* M = oz2::moduli(cfg.moduli);
-        for (int64_t c = 0; c < nc;) {
-            int64_t w = std::min(chunk, nc - c);
-            if (nc - c - w > 0 && nc - c - w < 1024) w = nc - c;  // absorb a narrow tail (src/chpl_single.cu:637-639)
-            // the body of chpl_oz2_gemm, unrolled here to time split and GEMM separately
-            const oz2::Layout y = oz2::layout((size_t)mt, (size_t)w, (size_t)nb, cfg.moduli, true, false);
-            uint8_t* pa = static_cast<uint8_t*>(wA[k & 1]);
-            uint8_t* pb = static_cast<uint8_t*>(work) + y.b_off;
-            int32_t* shA = reinterpret_cast<int32_t*>(pa + y.a_shift);
-            int8_t* resA = reinterpret_cast<int8_t*>(pa + y.a_res);
-            int32_t* shB = reinterpret_cast<int32_t*>(pb + y.b_shift);
-            int8_t* resB = reinterpret_cast<int8_t*>(pb + y.b_res);
-            void* tmp = static_cast<uint8_t*>(work) + y.tmp_off;
-            CHPL_TRY(clk.begin(st, PH_SPLIT, r));
-            if (split_a && c == 0) {
-                CHPL_TRY(oz2::split(st, false, at(jp + nb, jp), (size_t)ld, (size_t)mt, (size_t)nb, cfg.moduli, M->alpha,
-                                    resA, y.mPad, y.kPad, shA, tmp));
-                n_launch += 4;
-            }
-            CHPL_TRY(oz2::split(st, true, at(jp, c0 + c), (size_t)ld, (size_t)w, (size_t)nb, cfg.moduli, M->beta, resB,
-                                y.nPad, y.kPad, shB, tmp));
-            ++n_launch;
-            CHPL_TRY(clk.end(st, r));
-            PhaseTimer::Rec g;
-            CHPL_TRY(clk.begin(st, PH_GEMM, g));
-            CHPL_TRY(oz2::gemm_launch(st, 0, (size_t)mt, (size_t)w, y.kPad, cfg.moduli, resA, y.mPad, resB, y.nPad, shA,
-                                      shB, mone, one, at(jp + nb, c0 + c), (size_t)ld, nullptr, 0,
-                                      reinterpret_cast<int8_t*>(static_cast<uint8_t*>(work) + y.scratch_off),
-                                      y.grid_max));
-            CHPL_TRY(clk.end(st, g));
-            gemm_recs.push_back(g);
-            ++n_launch;
-            gemm_ops += 2.0 * (double)mt * (double)w * (double)y.kPad * cfg.moduli;
-            gemm_flops += 2.0 * (double)mt * (double)w * (double)nb;
-            ++n_emu;
-            c += w;
-        }
-        return CHPL_OK;
-    }
-
     int wait(cudaStream_t waiter, cudaStream_t producer)
     {
         if (waiter == producer) return CHPL_OK;
@@ -309,34 +254,202 @@ struct Solver {
         return CHPL_OK;
     }
 
-    // Step k.  sP: urgent update of panel k+1's columns (splits L21 once),
-    // then factor panel k+1.  s0: interchanges + U12 of the remaining columns,
-    // then the update of panel k+2's columns ("head", signalled to sP), then
-    // the rest.  Without lookahead sP == s0 and the same order runs serially.
+    // C[:, c0:c0+nc] -= L21 * U12 with L21 = A(r0:N, a0:a0+k), U12 = A(a0:a0+k, c0:c0+nc),
+    // C = A(r0:N, ...).  wa: A part of the residues (split here when split_a).
+    int update(cudaStream_t st, cublasHandle_t hb, void* work, void* wa, bool split_a, int64_t r0, int64_t a0,
+               int64_t k, int64_t c0, int64_t nc, int grid_cap)
+    {
+        return emu(st, hb, work, wa, split_a, N - r0, k, at(r0, a0), ld, a0, c0, nc, at(r0, c0), -1.0, 1.0, grid_cap);
+    }
+
+    // C(mt x nc) = alpha * Am(mt x k) * A(a0:a0+k, c0:c0+nc) + beta * C, C at Cp (ld).
+    // B is split completely before the GEMM kernel writes C, so C may alias B
+    // when beta == 0 (the kernel never reads B or, with beta == 0, C).
+    int emu(cudaStream_t st, cublasHandle_t hb, void* work, void* wa, bool split_a, int64_t mt, int64_t k,
+            const double* Am, int64_t lda_m, int64_t a0, int64_t c0, int64_t nc, double* Cp, double alpha, double beta,
+            int grid_cap)
+    {
+        if (nc <= 0 || mt <= 0 || k <= 0) return CHPL_OK;
+        const double one = beta, mone = alpha;
+        PhaseTimer::Rec r;
+        if (!cfg.emulate) {
+            CHPL_TRY(clk.begin(st, PH_UPD_FP64, r));
+            CHPL_CUBLAS(cublasDgemm_64(hb, CUBLAS_OP_N, CUBLAS_OP_N, mt, nc, k, &mone, Am, lda_m, at(a0, c0), ld, &one, Cp,
+                                       ld));
+            CHPL_TRY(clk.end(st, r));
+            return CHPL_OK;
+        }
+        const oz2::Moduli* M = oz2::moduli(cfg.moduli);
+        for (int64_t c = 0; c < nc;) {
+            int64_t w = std::min(chunk, nc - c);
+            if (nc - c - w > 0 && nc - c - w < 1024) w = nc - c;  // absorb a narrow tail (src/chpl_single.cu:637-639)
+            // the body of chpl_oz2_gemm, unrolled here to time split and GEMM separately
+            const oz2::Layout y = oz2::layout((size_t)mt, (size_t)w, (size_t)k, cfg.moduli, true, false, grid_cap);
+            uint8_t* pa = static_cast<uint8_t*>(wa);
+            uint8_t* pb = static_cast<uint8_t*>(work) + y.b_off;
+            int32_t* shA = reinterpret_cast<int32_t*>(pa + y.a_shift);
+            int8_t* resA = reinterpret_cast<int8_t*>(pa + y.a_res);
+            int32_t* shB = reinterpret_cast<int32_t*>(pb + y.b_shift);
+            int8_t* resB = reinterpret_cast<int8_t*>(pb + y.b_res);
+            void* tmp = static_cast<uint8_t*>(work) + y.tmp_off;
+            CHPL_TRY(clk.begin(st, PH_SPLIT, r));
+            if (split_a && c == 0) {
+                CHPL_TRY(oz2::split(st, false, Am, (size_t)lda_m, (size_t)mt, (size_t)k, cfg.moduli, M->alpha, resA,
+                                    y.mPad, y.kPad, shA, tmp));
+                n_launch += 4;
+            }
+            CHPL_TRY(oz2::split(st, true, at(a0, c0 + c), (size_t)ld, (size_t)w, (size_t)k, cfg.moduli, M->beta, resB,
+                                y.nPad, y.kPad, shB, tmp));
+            ++n_launch;
+            CHPL_TRY(clk.end(st, r));
+            PhaseTimer::Rec g;
+            CHPL_TRY(clk.begin(st, PH_GEMM, g));
+            CHPL_TRY(oz2::gemm_launch(st, 0, (size_t)mt, (size_t)w, y.kPad, cfg.moduli, resA, y.mPad, resB, y.nPad, shA,
+                                      shB, mone, one, Cp + (size_t)c * ld, (size_t)ld, nullptr, 0,
+                                      reinterpret_cast<int8_t*>(static_cast<uint8_t*>(work) + y.scratch_off),
+                                      y.grid_max));
+            CHPL_TRY(clk.end(st, g));
+            gemm_recs.push_back(g);
+            ++n_launch;
+            gemm_ops += 2.0 * (double)mt * (double)w * (double)y.kPad * cfg.moduli;
+            gemm_flops += 2.0 * (double)mt * (double)w * (double)k;
+            ++n_emu;
+            c += w;
+        }
+        return CHPL_OK;
+    }
+
+    int laswp_cols(cudaStream_t st, void* plan, int64_t nswaps, int64_t c0, int64_t nc)
+    {
+        if (nc <= 0) return CHPL_OK;
+        PhaseTimer::Rec r;
+        CHPL_TRY(clk.begin(st, PH_LASWP, r));
+        CHPL_TRY(laswp_apply(st, A, (size_t)ld, c0, nc, nswaps, plan));
+        ++n_launch;
+        CHPL_TRY(clk.end(st, r));
+        return CHPL_OK;
+    }
+
+    int trsm(cudaStream_t st, cublasHandle_t hb, int64_t d0, int64_t kd, int64_t c0, int64_t nc)
+    {
+        if (nc <= 0 || kd <= 0) return CHPL_OK;
+        const double one = 1.0;
+        PhaseTimer::Rec r;
+        CHPL_TRY(clk.begin(st, PH_TRSM, r));
+        CHPL_CUBLAS(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, kd, nc,
+                                   &one, at(d0, d0), ld, at(d0, c0), ld));
+        CHPL_TRY(clk.end(st, r));
+        return CHPL_OK;
+    }
+
+    int64_t sb_start(int64_t s) const { return s * K; }
+    int64_t sb_width(int64_t s) const { return std::max<int64_t>(0, std::min(K, N - s * K)); }
+
+    // Factor super-block s (columns [J, J+KJ), all rows below J) on sP: per
+    // panel, FP64 getrf, its interchanges on the super-block's other columns
+    // (left: L columns the bulk update reads; right: columns still to factor),
+    // U12 of the panel row and the inner update of the super-block's
+    // remaining columns.
+    int factor_superblock(int64_t s, int cap)
+    {
+        const int64_t J = sb_start(s), KJ = sb_width(s);
+        for (int64_t p = 0; J + p * NB < J + KJ; ++p) {
+            const int64_t jp = J + p * NB, nb = std::min(NB, J + KJ - jp);
+            void* plan = lw[s & 1][p];
+            PhaseTimer::Rec r;
+            CHPL_TRY(clk.begin(sP, PH_PANEL, r));
+            CHPL_CUSOLVER(cusolverDnXgetrf(hs, hp, N - jp, nb, CUDA_R_64F, at(jp, jp), ld, ipiv_rel, CUDA_R_64F, fwork_d,
+                                           fwd, fwork_h, fwh, info + 1));
+            CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
+            CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, plan));
+            n_launch += 2;
+            CHPL_TRY(clk.end(sP, r));
+            CHPL_TRY(laswp_cols(sP, plan, nb, J, jp - J));
+            const int64_t c0 = jp + nb, nc = J + KJ - c0;
+            CHPL_TRY(laswp_cols(sP, plan, nb, c0, nc));
+            CHPL_TRY(trsm(sP, hbP, jp, nb, c0, nc));
+            CHPL_TRY(update(sP, hbP, wP, wAin, true, jp + nb, jp, nb, c0, nc, cap));
+        }
+        return invert_l(s);
+    }
+
+    // trailing work of super-block s on columns [c0, c0+nc): interchanges and U12
+    int trailing_swap_trsm(cudaStream_t st, cublasHandle_t hb, int64_t s, int64_t c0, int64_t nc)
+    {
+        const int64_t J = sb_start(s), KJ = sb_width(s);
+        for (int64_t p = 0; J + p * NB < J + KJ; ++p)
+            CHPL_TRY(laswp_cols(st, lw[s & 1][p], std::min(NB, J + KJ - (J + p * NB)), c0, nc));
+        if (!emu_trsm) return trsm(st, hb, J, KJ, c0, nc);
+        // U12 = inv(L) * A12 in place (beta = 0: the kernel writes C from residues only)
+        return emu(st, hb, st == s0 ? w0 : wP, wLinv[s & 1], false, KJ, KJ, Linv[s & 1], KJ, J, c0, nc, at(J, c0), 1.0,
+                   0.0, st == s0 ? cap_bulk_cur : cap_chain_cur);
+    }
+
+    // inv(L) of super-block s (unit lower KJ x KJ at A(J, J)), then its residues
+    int invert_l(int64_t s)
+    {
+        if (!emu_trsm) return CHPL_OK;
+        const int64_t J = sb_start(s), KJ = sb_width(s);
+        double* Li = Linv[s & 1];
+        PhaseTimer::Rec r;
+        CHPL_TRY(clk.begin(sP, PH_TRSM, r));
+        CHPL_TRY(identity(sP, Li, KJ));
+        const double one = 1.0;
+        CHPL_CUBLAS(cublasDtrsm_64(hbP, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, KJ, KJ,
+                                   &one, at(J, J), ld, Li, KJ));
+        CHPL_TRY(clk.end(sP, r));
+        const oz2::Moduli* M = oz2::moduli(cfg.moduli);
+        const oz2::Layout y = oz2::layout((size_t)KJ, 256, (size_t)KJ, cfg.moduli, true, false);
+        uint8_t* pa = static_cast<uint8_t*>(wLinv[s & 1]);
+        CHPL_TRY(clk.begin(sP, PH_SPLIT, r));
+        CHPL_TRY(oz2::split(sP, false, Li, (size_t)KJ, (size_t)KJ, (size_t)KJ, cfg.moduli, M->alpha,
+                            reinterpret_cast<int8_t*>(pa + y.a_res), y.mPad, y.kPad, reinterpret_cast<int32_t*>(pa + y.a_shift),
+                            static_cast<uint8_t*>(wP) + y.tmp_off));
+        n_launch += 5;
+        CHPL_TRY(clk.end(sP, r));
+        return CHPL_OK;
+    }
+    int cap_bulk_cur = 0, cap_chain_cur = 0;
+
+    // Super-block s.  sP: urgent update of super-block s+1's columns (splits
+    // L21 once), then factor super-block s+1.  s0: interchanges + U12 of the
+    // remaining columns, then the update of super-block s+2's columns ("head",
+    // signalled to sP), then the rest.  Without lookahead sP == s0.
+    // The bulk update of super-block s runs beside the chain only when it is
+    // long enough to hide it: then the persistent GEMM of the bulk leaves
+    // `reserve` SMs free and the chain's GEMMs use only those.
+    bool overlapped(int64_t s) const
+    {
+        const int64_t c2 = std::min(N, sb_start(s) + sb_width(s) + sb_width(s + 1));
+        return cfg.lookahead && reserve > 0 && (N - c2) >= 8 * K;
+    }
+
     int factor_and_solve()
     {
-        const int64_t npan = (N + NB - 1) / NB;
-        CHPL_TRY(panel(0));
-        cudaEvent_t ev_head = nullptr;  // bulk(k-1) finished panel k+1's columns
-        for (int64_t k = 0; k < npan; ++k) {
-            const int64_t jp = k * NB, nb = std::min(NB, N - jp);
-            const int64_t c1 = jp + nb;                                   // panel k+1's first column
-            const int64_t nb1 = std::max<int64_t>(0, std::min(NB, N - c1));
-            const int64_t c2 = c1 + nb1;                                  // panel k+2's first column
-            const int64_t nb2 = std::max<int64_t>(0, std::min(NB, N - c2));
-            // urgent (sP): columns of panel k+1 must have received step k-1 first
+        const int64_t nsb = (N + K - 1) / K;
+        CHPL_TRY(factor_superblock(0, 0));
+        cudaEvent_t ev_head = nullptr;   // bulk(s-1) finished super-block s+1's columns
+        for (int64_t s = 0; s < nsb; ++s) {
+            const int64_t J = sb_start(s), KJ = sb_width(s);
+            const int64_t c1 = J + KJ, K1 = sb_width(s + 1);
+            const int64_t c2 = c1 + K1, K2 = std::max<int64_t>(0, std::min(K, N - c2));
+            const int cap_prev = (s > 0 && overlapped(s - 1)) ? reserve : 0;   // urgent(s) runs beside bulk(s-1)
+            const int cap_chain = overlapped(s) ? reserve : 0;                 // factor(s+1) runs beside bulk(s)
+            const int cap_bulk = overlapped(s) ? nsm - reserve : 0;
+            cap_bulk_cur = cap_bulk;
+            cap_chain_cur = cap_prev;
             if (ev_head) CHPL_CUDA(cudaStreamWaitEvent(sP, ev_head, 0));
-            CHPL_TRY(swap_trsm(sP, hbP, k, c1, nb1));
-            CHPL_TRY(gemm(sP, hbP, wP, k, c1, nb1, true));
-            const bool a_split = nb1 > 0 && N - c1 > 0;
-            // bulk (s0) needs panel k factored and L21 split by the urgent update
+            CHPL_TRY(trailing_swap_trsm(sP, hbP, s, c1, K1));
+            CHPL_TRY(update(sP, hbP, wP, wA[s & 1], true, c1, J, KJ, c1, K1, cap_prev));
+            const bool a_split = K1 > 0 && N - c1 > 0;
             CHPL_TRY(wait(s0, sP));
-            if (nb1 > 0) CHPL_TRY(panel(k + 1));
-            CHPL_TRY(swap_trsm(s0, hb0, k, c2, ncols - c2));
-            CHPL_TRY(gemm(s0, hb0, w0, k, c2, nb2, !a_split));
+            cap_chain_cur = cap_chain;
+            if (K1 > 0) CHPL_TRY(factor_superblock(s + 1, cap_chain));
+            CHPL_TRY(trailing_swap_trsm(s0, hb0, s, c2, ncols - c2));
+            CHPL_TRY(update(s0, hb0, w0, wA[s & 1], !a_split, c1, J, KJ, c2, K2, cap_bulk));
             ev_head = event();
             CHPL_CUDA(cudaEventRecord(ev_head, s0));
-            CHPL_TRY(gemm(s0, hb0, w0, k, c2 + nb2, ncols - c2 - nb2, !a_split && nb2 == 0));
+            CHPL_TRY(update(s0, hb0, w0, wA[s & 1], !a_split && K2 == 0, c1, J, KJ, c2 + K2, ncols - c2 - K2, cap_bulk));
         }
         CHPL_TRY(wait(s0, sP));
         PhaseTimer::Rec r;
@@ -368,6 +481,7 @@ int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_o
     if (!cfg || !res) { set_error("cfg/res NULL"); return CHPL_ERR_INVALID; }
     std::memset(res, 0, sizeof(*res));
     if (cfg->N <= 0 || cfg->NB <= 0 || cfg->NB > 2048) { set_error("bad N/NB (NB must be in [1, 2048])"); return CHPL_ERR_INVALID; }
+    if (cfg->agg < 0 || (int64_t)cfg->agg * cfg->NB > 16384) { set_error("agg * NB must be <= 16384"); return CHPL_ERR_INVALID; }
     if (cfg->P != 1 || cfg->Q != 1) { set_error("chpl_hpl_run drives one GPU; use the grid driver for P x Q > 1"); return CHPL_ERR_INVALID; }
     if (cfg->emulate && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
     Solver s;
@@ -432,6 +546,8 @@ extern "C" void chpl_hpl_default_config(chpl_hpl_config* cfg)
     cfg->fast = 1;
     cfg->chunk = 0;
     cfg->lookahead = 1;
+    cfg->agg = 0;
+    cfg->reserve_sms = -1;
     cfg->seed = 42;
     cfg->threshold = 16.0;
     cfg->verbose = 0;

@@ -85,6 +85,9 @@ class Config:
     fast: bool = True
     chunk: int = 0
     lookahead: bool = True
+    agg: int = 0
+    reserve_sms: int = -1
+    trsm_mode: int = 0
     seed: int = 42
     threshold: float = 16.0
     verbose: bool = False
@@ -94,13 +97,14 @@ class Config:
         c.N, c.NB, c.P, c.Q = self.N, self.NB, self.P, self.Q
         c.moduli, c.emulate, c.fast, c.chunk = self.moduli, int(self.emulate), int(self.fast), self.chunk
         c.lookahead, c.seed, c.threshold, c.verbose = int(self.lookahead), self.seed, self.threshold, int(self.verbose)
+        c.agg, c.reserve_sms, c.trsm_mode = self.agg, self.reserve_sms, self.trsm_mode
         return c
 
 
 def single_config_from_env(N: int, env=None) -> Config:
     """chpl_single's configuration (src/chpl_single.cu:842-869, launcher defaults
-    scripts/mpirun_chpl:71-76).  HPLS_AGG is accepted for compatibility: the
-    fused emulated update needs no K aggregation, so it is ignored."""
+    scripts/mpirun_chpl:71-76).  HPLS_AGG groups panels into super-blocks whose
+    trailing update runs with k = AGG * NB (0 = automatic, k = 4096)."""
     env = os.environ if env is None else env
     backend = env.get("HPLS_BACKEND", "gemmul8")
     if backend not in ("native", "gemmul8", "ozaki"):
@@ -108,7 +112,7 @@ def single_config_from_env(N: int, env=None) -> Config:
     c = Config(N=N, NB=_env_int(env, "HPLS_NB", 1024), moduli=_env_int(env, "HPLS_G8_MODULI", 11),
                emulate=backend != "native", fast=bool(_env_int(env, "HPLS_G8_FAST", 1)),
                chunk=_env_int(env, "HPLS_G8_CHUNK", 0), seed=_env_int(env, "HPLS_SEED", 42),
-               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 1)))
+               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 1)), agg=_env_int(env, "HPLS_AGG", 0))
     if c.N <= 0 or c.NB <= 0 or c.NB > c.N:
         raise ValueError("bad N/NB")
     return c

@@ -36,7 +36,7 @@ _dp = ctypes.POINTER(ctypes.c_double)
 
 class HplConfig(ctypes.Structure):
     _fields_ = [("N", _i64), ("NB", _i64), ("P", _int), ("Q", _int), ("moduli", _int), ("emulate", _int),
-                ("fast", _int), ("chunk", _i64), ("lookahead", _int), ("agg", _int), ("reserve_sms", _int), ("trsm_mode", _int),
+                ("fast", _int), ("chunk", _i64), ("lookahead", _int), ("agg", _int), ("reserve_sms", _int), ("trsm_mode", _int), ("panel_mode", _int),
                 ("seed", _u64), ("threshold", _dbl), ("verbose", _int)]
 
 

@@ -38,6 +38,32 @@ def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool) -> dict:
             "kernel_int8_tops": 2.0 * m * n * (-(-k // 128) * 128) * L / best[1] / 1e12}
 
 
+def panel_case(m: int, n: int, reps: int) -> dict:
+    import ctypes
+
+    from . import _lib
+    L = _lib.load()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    A0 = torch.rand(n, m, dtype=torch.float64, device="cuda", generator=g) - 0.5   # column-major m x n
+    A = A0.clone()
+    piv = torch.zeros(n, dtype=torch.int64, device="cuda")
+    info = torch.zeros(1, dtype=torch.int32, device="cuda")
+    work = torch.empty(L.chpl_panel_getrf_work_bytes(m, n), dtype=torch.uint8, device="cuda")
+    best = 1e30
+    for _ in range(reps):
+        A.copy_(A0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _lib.check(L.chpl_panel_getrf_f64(0, m, n, A.data_ptr(), m, piv.data_ptr(), info.data_ptr(), work.data_ptr()),
+                   "chpl_panel_getrf_f64")
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e-3)
+    fl = m * n * n - n ** 3 / 3.0
+    return {"case": "panel", "m": m, "n": n, "ms": best * 1e3, "fp64_tflops": fl / best / 1e12, "info": int(info.item())}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -48,6 +74,10 @@ def main() -> None:
     g.add_argument("--moduli", type=int, default=11)
     g.add_argument("--reps", type=int, default=3)
     g.add_argument("--scaled", action="store_true")
+    pn = sub.add_parser("panel")
+    pn.add_argument("--m", type=int, default=65536)
+    pn.add_argument("--n", type=int, default=1024)
+    pn.add_argument("--reps", type=int, default=3)
     h = sub.add_parser("hpl")
     h.add_argument("--N", type=int, default=16384)
     h.add_argument("--NB", type=int, default=1024)
@@ -57,15 +87,20 @@ def main() -> None:
     h.add_argument("--agg", type=int, default=0)
     h.add_argument("--trsm-mode", type=int, default=0)
     h.add_argument("--reserve", type=int, default=-1)
+    h.add_argument("--panel-mode", type=int, default=0)
+    h.add_argument("--lookahead", action="store_true")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.what == "gemm":
         print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled)), flush=True)
+    elif a.what == "panel":
+        print(json.dumps(panel_case(a.m, a.n, a.reps)), flush=True)
     else:
-        r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=not a.no_lookahead, emulate=not a.fp64,
-                               agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve))
+        r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=a.lookahead and not a.no_lookahead,
+                               emulate=not a.fp64, agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve,
+                               panel_mode=a.panel_mode))
         print(json.dumps({"case": "hpl", "N": a.N, "NB": a.NB, "agg": a.agg, "trsm_mode": a.trsm_mode,
-                          "lookahead": not a.no_lookahead, "tflops": r.tflops, "time_s": r.time_s,
+                          "lookahead": a.lookahead, "panel_mode": a.panel_mode, "tflops": r.tflops, "time_s": r.time_s,
                           "resid": r.resid, "passed": r.passed, "phases": r.phases,
                           "gemm_int8_tops": r.gemm_int8_ops / r.gemm_kernel_s / 1e12 if r.gemm_kernel_s else None,
                           "gemm_launches": r.gemm_launches}), flush=True)

@@ -21,11 +21,17 @@ static inline int64_t local_extent(int64_t n, int64_t nb, int P, int p)
 int matgen(cudaStream_t st, double* A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0, int64_t ncg,
            uint64_t seed);
 size_t laswp_work_bytes(int64_t nswaps);
-int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work);
+// plan the swaps (i <-> ipiv[i] - pbase), i = k1..k2-1, into `work`
+int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work, int64_t pbase = 0);
 int laswp_apply(cudaStream_t st, double* A, size_t lda, int64_t c0, int64_t ncols, int64_t nswaps, const void* work);
 int ipiv_to_abs(cudaStream_t st, const int64_t* rel, int64_t n, int64_t base, int64_t* out);
 int identity(cudaStream_t st, double* X, int64_t n);
 int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid);
 int hpl_read_clear_status(int* st);
+size_t panel_work_bytes(int64_t m, int64_t n);
+// FP64 getrf of the m x n panel at A; ipiv[i] = base_row + pivot row within the panel
+int panel_getrf(cudaStream_t st, int64_t m, int64_t n, double* A, size_t lda, int64_t* ipiv, int64_t base_row, int* info,
+                void* work);
+int panel_status(void* work, int* err);
 
 }  // namespace chpl

@@ -83,8 +83,8 @@ constexpr int kHash = 4096;  // power of two >= 2 * kLaswpMaxSwaps / 1 (load fac
 constexpr size_t kPlanSmem = (size_t)kHash * 4 * 2 + (size_t)2 * kLaswpMaxSwaps * 4 * 2 + (size_t)kLaswpMaxSwaps * 4 + 16;
 
 __global__ void __launch_bounds__(1024) laswp_plan_kernel(const int64_t* __restrict__ ipiv, long long k1, int ns,
-                                                          int* __restrict__ dst, int* __restrict__ src,
-                                                          int* __restrict__ cnt)
+                                                          long long pbase, int* __restrict__ dst,
+                                                          int* __restrict__ src, int* __restrict__ cnt)
 {
     extern __shared__ int psm[];
     int* key = psm;                              // [kHash] row ids >= k2, -1 = empty
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(1024) laswp_plan_kernel(const int64_t* __restr
     if (threadIdx.x == 0) { counters[0] = 0; counters[1] = 0; }
     __syncthreads();
     for (int i = threadIdx.x; i < ns; i += blockDim.x) {
-        const int p = (int)ipiv[k1 + i];
+        const int p = (int)(ipiv[k1 + i] - pbase);
         if (p < k2) { pslot[i] = (int)(p - k1); continue; }
         unsigned h = ((unsigned)p * 2654435761u) & (kHash - 1);
         while (true) {
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(256) laswp_apply_kernel(double* __restrict__ A
 
 size_t laswp_work_bytes(int64_t nswaps) { return round_up((size_t)(2 * nswaps) * 8 + 64, 256); }
 
-int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work)
+int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, void* work, int64_t pbase)
 {
     const int ns = (int)(k2 - k1);
     if (ns <= 0) return CHPL_OK;
@@ -178,7 +178,7 @@ int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, voi
     int* dst = cnt + 16;
     int* src = dst + 2 * ns;
     CHPL_CUDA(cudaFuncSetAttribute(laswp_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlanSmem));
-    laswp_plan_kernel<<<1, 1024, kPlanSmem, st>>>(ipiv, (long long)k1, ns, dst, src, cnt);
+    laswp_plan_kernel<<<1, 1024, kPlanSmem, st>>>(ipiv, (long long)k1, ns, (long long)pbase, dst, src, cnt);
     CHPL_CUDA(cudaGetLastError());
     return CHPL_OK;
 }

@@ -99,6 +99,7 @@ struct Solver {
     int* info = nullptr;
     void* fwork_d = nullptr;
     void* fwork_h = nullptr;
+    void* pwork = nullptr;                 // workspace of the FP64 panel kernel
     size_t fwd = 0, fwh = 0;
     std::vector<void*> lw[2];              // laswp plans of the panels of a super-block, by super-block parity
     void* wA[2] = {nullptr, nullptr};      // residues of a super-block's L21 (k = K), by parity, shared by streams
@@ -195,6 +196,7 @@ struct Solver {
         CHPL_CUDA(cudaMemset(info, 0, 64 * sizeof(int)));
         CHPL_CUDA(cudaMalloc(&fwork_d, fwd ? fwd : 8));
         fwork_h = std::malloc(fwh ? fwh : 8);
+        CHPL_CUDA(cudaMalloc(&pwork, panel_work_bytes(N, NB)));
         for (int b = 0; b < 2; ++b) {
             lw[b].assign(npl, nullptr);
             for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw[b][p], laswp_work_bytes(NB)));
@@ -232,6 +234,7 @@ struct Solver {
             for (void* p : lw[b]) if (p) cudaFree(p);
         }
         if (fwork_d) cudaFree(fwork_d);
+        if (pwork) cudaFree(pwork);
         std::free(fwork_h);
         if (info) cudaFree(info);
         if (ipiv) cudaFree(ipiv);
@@ -358,9 +361,14 @@ struct Solver {
             void* plan = lw[s & 1][p];
             PhaseTimer::Rec r;
             CHPL_TRY(clk.begin(sP, PH_PANEL, r));
-            CHPL_CUSOLVER(cusolverDnXgetrf(hs, hp, N - jp, nb, CUDA_R_64F, at(jp, jp), ld, ipiv_rel, CUDA_R_64F, fwork_d,
-                                           fwd, fwork_h, fwh, info + 1));
-            CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
+            if (cfg.panel_mode == 1) {
+                CHPL_CUSOLVER(cusolverDnXgetrf(hs, hp, N - jp, nb, CUDA_R_64F, at(jp, jp), ld, ipiv_rel, CUDA_R_64F,
+                                               fwork_d, fwd, fwork_h, fwh, info + 1));
+                CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
+            } else {
+                CHPL_TRY(panel_getrf(sP, N - jp, nb, at(jp, jp), (size_t)ld, ipiv + jp, jp, info + 1, pwork));
+                n_launch += 2 * ((nb + 15) / 16) * 2;
+            }
             CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, plan));
             n_launch += 2;
             CHPL_TRY(clk.end(sP, r));
@@ -507,6 +515,9 @@ int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_o
     cudaEventElapsedTime(&ms, t0, t1);
     int hinfo = 0;
     cudaMemcpy(&hinfo, s.info + 1, sizeof(int), cudaMemcpyDeviceToHost);
+    int perr = 0;
+    if (s.pwork) panel_status(s.pwork, &perr);
+    if (perr) { set_error("device-side timeout in the panel factorization"); return finish(CHPL_ERR_TIMEOUT); }
     int dstat = 0;
     oz2::read_clear_status(&dstat);
     if (dstat) { set_error("device-side timeout in the emulated update"); return finish(CHPL_ERR_TIMEOUT); }
@@ -545,7 +556,7 @@ extern "C" void chpl_hpl_default_config(chpl_hpl_config* cfg)
     cfg->emulate = 1;
     cfg->fast = 1;
     cfg->chunk = 0;
-    cfg->lookahead = 1;
+    cfg->lookahead = 0;
     cfg->agg = 0;
     cfg->reserve_sms = -1;
     cfg->seed = 42;

@@ -84,10 +84,11 @@ class Config:
     emulate: bool = True
     fast: bool = True
     chunk: int = 0
-    lookahead: bool = True
+    lookahead: bool = False
     agg: int = 0
     reserve_sms: int = -1
     trsm_mode: int = 0
+    panel_mode: int = 0
     seed: int = 42
     threshold: float = 16.0
     verbose: bool = False
@@ -97,7 +98,7 @@ class Config:
         c.N, c.NB, c.P, c.Q = self.N, self.NB, self.P, self.Q
         c.moduli, c.emulate, c.fast, c.chunk = self.moduli, int(self.emulate), int(self.fast), self.chunk
         c.lookahead, c.seed, c.threshold, c.verbose = int(self.lookahead), self.seed, self.threshold, int(self.verbose)
-        c.agg, c.reserve_sms, c.trsm_mode = self.agg, self.reserve_sms, self.trsm_mode
+        c.agg, c.reserve_sms, c.trsm_mode, c.panel_mode = self.agg, self.reserve_sms, self.trsm_mode, self.panel_mode
         return c
 
 
@@ -112,7 +113,7 @@ def single_config_from_env(N: int, env=None) -> Config:
     c = Config(N=N, NB=_env_int(env, "HPLS_NB", 1024), moduli=_env_int(env, "HPLS_G8_MODULI", 11),
                emulate=backend != "native", fast=bool(_env_int(env, "HPLS_G8_FAST", 1)),
                chunk=_env_int(env, "HPLS_G8_CHUNK", 0), seed=_env_int(env, "HPLS_SEED", 42),
-               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 1)), agg=_env_int(env, "HPLS_AGG", 0))
+               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 0)), agg=_env_int(env, "HPLS_AGG", 0))
     if c.N <= 0 or c.NB <= 0 or c.NB > c.N:
         raise ValueError("bad N/NB")
     return c
@@ -124,7 +125,7 @@ def grid_config_from_env(dat: HplDat, P: int, Q: int, env=None) -> Config:
     return Config(N=dat.N, NB=dat.NB, P=P, Q=Q, threshold=dat.threshold,
                   emulate=bool(_env_int(env, "CHPL2D_G8", 1)), moduli=_env_int(env, "CHPL2D_G8_MODULI", 11),
                   fast=bool(_env_int(env, "CHPL2D_G8_FAST", 1)), chunk=_env_int(env, "CHPL2D_G8_NT", 0),
-                  lookahead=bool(_env_int(env, "CHPL2D_LOOKAHEAD", 1)))
+                  lookahead=bool(_env_int(env, "CHPL2D_LOOKAHEAD", 0)))
 
 
 @dataclass

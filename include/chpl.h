@@ -193,12 +193,13 @@ typedef struct chpl_hpl_config {
     int emulate;        /* CHPL2D_G8 / HPLS_BACKEND=gemmul8: 1 = Ozaki-II update, 0 = FP64 */
     int fast;           /* CHPL2D_G8_FAST / HPLS_G8_FAST */
     int64_t chunk;      /* column chunk of the update (CHPL2D_G8_NT / HPLS_G8_CHUNK), 0 = auto */
-    int lookahead;      /* depth-1 lookahead on a high-priority stream (1) or serial (0) */
+    int lookahead;      /* depth-1 lookahead on a high-priority stream (1) or serial (0, default) */
     int agg;            /* HPLS_AGG: panels per super-block; the bulk update runs with k = agg * NB
                            (src/chpl_single.cu:662); 0 = auto (k = 4096) */
     int reserve_sms;    /* SMs left to the lookahead chain while the bulk update runs; -1 = auto */
     int trsm_mode;      /* U12 of a super-block: 0 = auto, 1 = inv(L) * A12 through the emulated GEMM,
                            2 = FP64 triangular solve */
+    int panel_mode;     /* 0 = this library's FP64 panel kernel, 1 = cuSOLVER getrf (comparison) */
     uint64_t seed;      /* 42 */
     double threshold;   /* HPL.dat line 13 (16.0) */
     int verbose;        /* print progress lines */

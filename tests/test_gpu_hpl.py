@@ -69,7 +69,7 @@ def test_laswp_bitexact(cuda, case):
     assert np.array_equal(from_dev(dA, nrows, ncols), ref)
 
 
-@pytest.mark.parametrize("mn", [(1000, 128), (4096, 1024), (257, 64)])
+@pytest.mark.parametrize("mn", [(1000, 128), (4096, 1024), (257, 64), (300, 300), (65536, 160), (2000, 37)])
 def test_panel_getrf(cuda, mn):
     m, n = mn
     L = _lib.load()
@@ -87,6 +87,27 @@ def test_panel_getrf(cuda, mn):
     assert np.array_equal(piv.cpu().numpy(), p)
     got = from_dev(dA, m, n)
     assert np.allclose(got, lu, rtol=1e-11, atol=1e-12)
+
+
+def test_panel_getrf_zero_pivot(cuda):
+    """An exactly singular panel reports the first zero pivot (LAPACK info) without faulting."""
+    L = _lib.load()
+    m, n = 500, 48
+    A = np.random.default_rng(1).uniform(-0.5, 0.5, (m, n))
+    A[:, 5] = A[:, 2]                              # column 5 depends on column 2
+    dA, lda = to_dev(A)
+    piv = torch.zeros(n, dtype=torch.int64, device="cuda")
+    info = torch.zeros(1, dtype=torch.int32, device="cuda")
+    work = empty_bytes(L.chpl_panel_getrf_work_bytes(m, n))
+    _lib.check(L.chpl_panel_getrf_f64(0, m, n, dA.data_ptr(), lda, piv.data_ptr(), info.data_ptr(),
+                                      work.data_ptr()), "panel_getrf")
+    torch.cuda.synchronize()
+    _, p = scipy.linalg.lu_factor(A, check_finite=False)
+    assert np.array_equal(piv.cpu().numpy()[:5], p[:5])
+    # rounding may leave a tiny nonzero instead of an exact zero; an exact zero must give info = 6
+    got = from_dev(dA, m, n)
+    if got[5, 5] == 0.0:
+        assert info.item() == 6
 
 
 def test_residual_matches_oracle(cuda):
@@ -140,6 +161,15 @@ def test_hpl_ragged_sizes(cuda):
     """N not a multiple of NB, chunked update with tail absorption."""
     res = hpl.run(hpl.Config(N=2500, NB=192, moduli=12, chunk=700), want_x=True)
     assert res.passed, res.resid
+
+
+def test_hpl_panel_kernel_matches_cusolver_pivots(cuda):
+    """Own FP64 panel kernel vs cuSOLVER getrf inside the solver: same pivots, so
+    the same solution up to rounding."""
+    a = hpl.run(hpl.Config(N=3000, NB=512, moduli=12, panel_mode=0), want_x=True)
+    b = hpl.run(hpl.Config(N=3000, NB=512, moduli=12, panel_mode=1), want_x=True)
+    assert a.passed and b.passed
+    assert np.allclose(a.x, b.x, rtol=1e-6, atol=1e-9)
 
 
 def test_hpl_emulated_vs_oracle_small(cuda):

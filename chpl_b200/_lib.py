@@ -71,6 +71,12 @@ SIGNATURES = {
     "chpl_residual": (_int, [_vp, _i64, _u64, _vp, _dp]),
     "chpl_hpl_default_config": (None, [ctypes.POINTER(HplConfig)]),
     "chpl_hpl_run": (_int, [ctypes.POINTER(HplConfig), ctypes.POINTER(HplResult), _vp]),
+    "chpl_grid_unique_id": (_int, [_vp, _sz]),
+    "chpl_grid_create": (_int, [_int, _int, _int, _vp, _sz, _dbl, ctypes.POINTER(_vp)]),
+    "chpl_grid_run": (_int, [_vp, ctypes.POINTER(HplConfig), ctypes.POINTER(HplResult), _vp]),
+    "chpl_grid_destroy": (_int, [_vp]),
+    "chpl_grid_plan_exchange": (_int, [_i64, _i64, _vp, _i64, _int, _int, _vp, _vp, ctypes.POINTER(_int), _vp,
+                                       ctypes.POINTER(_int), _vp, ctypes.POINTER(_int)]),
 }
 
 _lib = None

@@ -27,8 +27,24 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
                   "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
 LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu", "hpl_grid.cu"]
-LINK = ["-cudart", "shared", "-lcublas", "-lcusolver", "-lnccl",
-        "-Xlinker", "-rpath," + os.path.join(CUDA, "lib64")]
+def _nccl_dir() -> str:
+    """NCCL bundled with torch (the same library torch.distributed loads), so
+    one NCCL lives in the process; falls back to the system copy."""
+    try:
+        import nvidia.nccl as _n  # noqa: F401
+        d = os.path.join(os.path.dirname(list(_n.__path__)[0]), "nccl")
+        if os.path.exists(os.path.join(d, "lib", "libnccl.so.2")):
+            return d
+    except ImportError:
+        pass
+    return ""
+
+
+NCCL_DIR = _nccl_dir()
+NCCL_INC = ["-I", os.path.join(NCCL_DIR, "include")] if NCCL_DIR else []
+NCCL_LINK = (["-L", os.path.join(NCCL_DIR, "lib"), "-l:libnccl.so.2", "-Xlinker", "-rpath," + os.path.join(NCCL_DIR, "lib")]
+             if NCCL_DIR else ["-lnccl"])
+LINK = ["-cudart", "shared", "-lcublas", "-lcusolver"] + NCCL_LINK + ["-Xlinker", "-rpath," + os.path.join(CUDA, "lib64")]
 EXES = {"chpl_single": "chpl_single_main.cpp", "chpl_p2": "chpl_p2_main.cpp"}
 
 
@@ -60,7 +76,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(BIN, exist_ok=True)
     hdrs = _headers()
-    flags = NVFLAGS + (extra_flags or [])
+    flags = NVFLAGS + NCCL_INC + (extra_flags or [])
     objs = []
     jobs = []
     for src in LIB_SOURCES:

@@ -1,1 +1,819 @@
-// Multi-GPU (P x Q) HPL driver.
+// Multi-GPU HPL on a P x Q process grid, one process per GPU (the chpl_p2
+// path of the reference, src/chpl_p2.cu, rebuilt for B200 + NCCL).
+//
+// Layout: 2D block-cyclic with block NB; rank r has pr = r % P, qc = r / P
+// (rank = P*qc + pr, src/chpl_p2.cu:528); global row block i lives on process
+// row i % P, column block j on process column j % Q.  Each rank holds one
+// column-major local array (lda = local rows rounded to 32).
+//
+// Per block column s (global columns [J, J+NB), J = s*NB; owner column
+// qs = s % Q, diagonal owner row ps = s % P):
+//   1. factor: the active rows of the block column are gathered onto
+//      (ps, qs) (for P = 2 the other process row sends its rows over NVLink),
+//      factored with exact partial pivoting (internal panels of width <= 1024,
+//      this library's FP64 panel kernel, inner updates through the emulated
+//      GEMM), then the factored rows are scattered back to their owners.
+//   2. pivots go to every rank (ncclBroadcast on the world communicator);
+//      inv(L11) and W = L21 go along process rows (row communicator).
+//   3. interchanges of the trailing columns: moves inside a rank are a local
+//      gather/scatter, moves across process rows an ncclSend/Recv pair on the
+//      column communicator.
+//   4. U12 = inv(L11) * A12 on process row ps (emulated GEMM, in place), then
+//      broadcast down the process columns (column communicator).
+//   5. A22 -= W * U12 locally (emulated GEMM).
+// Back substitution is distributed (per block: ncclReduce of partial sums on
+// the owning process row, trsv by the diagonal owner, ncclBroadcast of x_j on
+// the owning process column); the residual regenerates A locally and reduces
+// over process rows.  Communicators come from one unique id and
+// ncclCommSplit; a host watchdog aborts them (ncclCommAbort) if a step does
+// not finish within the configured timeout.
+#include <cublas_v2.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cinttypes>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+#include "hpl.h"
+#include "oz2.h"
+
+namespace chpl {
+
+#define CHPL_NCCL(call)                                                                                   \
+    do {                                                                                                  \
+        ncclResult_t r_ = (call);                                                                         \
+        if (r_ != ncclSuccess) {                                                                          \
+            set_error("NCCL error %d (%s) in %s at %s:%d", (int)r_, ncclGetErrorString(r_), #call, __FILE__, \
+                      __LINE__);                                                                          \
+            return CHPL_ERR_NCCL;                                                                         \
+        }                                                                                                 \
+    } while (0)
+#define CHPL_CUBLAS_G(call)                                                                               \
+    do {                                                                                                  \
+        cublasStatus_t s_ = (call);                                                                       \
+        if (s_ != CUBLAS_STATUS_SUCCESS) {                                                                \
+            set_error("cuBLAS error %d in %s at %s:%d", (int)s_, #call, __FILE__, __LINE__);              \
+            return CHPL_ERR_CUDA;                                                                         \
+        }                                                                                                 \
+    } while (0)
+
+// ---------------------------------------------------------------------------- kernels
+__global__ void rows_gather_kernel(double* __restrict__ dst, long long ldd, const double* __restrict__ A, long long lda,
+                                   const int* __restrict__ rows, int nrows, long long ncols)
+{
+    const long long total = (long long)nrows * ncols;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(e % nrows);
+        const long long c = e / nrows;
+        dst[t + c * ldd] = A[rows[t] + c * lda];
+    }
+}
+
+__global__ void rows_scatter_kernel(double* __restrict__ A, long long lda, const double* __restrict__ src, long long lds,
+                                    const int* __restrict__ rows, int nrows, long long ncols)
+{
+    const long long total = (long long)nrows * ncols;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(e % nrows);
+        const long long c = e / nrows;
+        A[rows[t] + c * lda] = src[t + c * lds];
+    }
+}
+
+// Gathered panel row r (global J + r) <-> its owner's local row.  dir = 0:
+// G <- (own A | partner's packed rows R); dir = 1: (own A | S for the
+// partner) <- G.  Owner of global row g: (g / NB) % P; its local row
+// (g / NB / P) * NB + g % NB; its first active local row lrb[p].
+__global__ void panel_shuffle_kernel(double* __restrict__ G, long long ldg, long long mg, long long ncols, long long J,
+                                     long long NB, int P, int me, double* __restrict__ Aown, long long lda,
+                                     long long lrb_me, double* __restrict__ R, long long ldr, long long lrb_other, int dir)
+{
+    const long long total = mg * ncols;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e % mg, c = e / mg;
+        const long long g = J + r, b = g / NB;
+        const int p = (int)(b % P);
+        const long long l = (b / P) * NB + g % NB;
+        double* src = (p == me) ? &Aown[(l - lrb_me) + c * lda] : &R[(l - lrb_other) + c * ldr];
+        if (dir == 0) G[r + c * ldg] = *src;
+        else *src = G[r + c * ldg];
+    }
+}
+
+__global__ void axpby_rows_kernel(double* __restrict__ v, const double* __restrict__ b, const double* __restrict__ t,
+                                  int n, int use_b)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) v[i] = (use_b ? b[i] : 0.0) - t[i];
+}
+
+__device__ __forceinline__ double grid_elem(uint64_t seed, uint64_t idx)
+{
+    uint64_t z = (idx + 1ull) * 0x9E3779B97F4A7C15ull + seed;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z = z ^ (z >> 31);
+    return (double)(z >> 11) * (1.0 / 9007199254740992.0) - 0.5;
+}
+
+// partial A x and row |A| sums over this rank's local columns (global < N),
+// chunked over columns for a deterministic two-stage sum
+constexpr int kGridResChunks = 16;
+__global__ void __launch_bounds__(256) grid_resid_partial_kernel(long long N, long long NB, int P, int Q, int pr, int qc,
+                                                                 long long mloc, long long nloc, uint64_t seed,
+                                                                 const double* __restrict__ x, double* __restrict__ part)
+{
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const int ch = blockIdx.y;
+    if (i >= mloc) return;
+    const long long gi = (i / NB * P + pr) * NB + i % NB;
+    const long long per = (nloc + kGridResChunks - 1) / kGridResChunks;
+    const long long c0 = ch * per, c1 = min(nloc, c0 + per);
+    double ax = 0.0, rs = 0.0;
+    for (long long c = c0; c < c1; ++c) {
+        const long long gc = (c / NB * Q + qc) * NB + c % NB;
+        if (gc >= N) continue;
+        const double a = grid_elem(seed, (uint64_t)gi * (uint64_t)(N + 1) + (uint64_t)gc);
+        ax = fma(a, x[gc], ax);
+        rs += fabs(a);
+    }
+    part[(ch * 2 + 0) * mloc + i] = ax;
+    part[(ch * 2 + 1) * mloc + i] = rs;
+}
+
+__global__ void grid_resid_sum_kernel(long long mloc, const double* __restrict__ part, double* __restrict__ axrs)
+{
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= mloc) return;
+    double ax = 0.0, rs = 0.0;
+    for (int c = 0; c < kGridResChunks; ++c) {
+        ax += part[(c * 2 + 0) * mloc + i];
+        rs += part[(c * 2 + 1) * mloc + i];
+    }
+    axrs[i] = ax;
+    axrs[mloc + i] = rs;
+}
+
+// per local row: |ax - b|, rs, |b| maxima into out[blk*3 + {0,1,2}]
+__global__ void __launch_bounds__(256) grid_resid_max_kernel(long long N, long long NB, int P, int pr, long long mloc,
+                                                             uint64_t seed, const double* __restrict__ axrs,
+                                                             double* __restrict__ out)
+{
+    __shared__ double sm[3][256];
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    double r = 0.0, rs = 0.0, ba = 0.0;
+    if (i < mloc) {
+        const long long gi = (i / NB * P + pr) * NB + i % NB;
+        const double b = grid_elem(seed, (uint64_t)gi * (uint64_t)(N + 1) + (uint64_t)N);
+        r = fabs(axrs[i] - b);
+        rs = axrs[mloc + i];
+        ba = fabs(b);
+    }
+    sm[0][threadIdx.x] = r; sm[1][threadIdx.x] = rs; sm[2][threadIdx.x] = ba;
+    __syncthreads();
+    for (int o = 128; o; o >>= 1) {
+        if (threadIdx.x < o)
+            for (int q = 0; q < 3; ++q) sm[q][threadIdx.x] = fmax(sm[q][threadIdx.x], sm[q][threadIdx.x + o]);
+        __syncthreads();
+    }
+    if (threadIdx.x < 3) out[blockIdx.x * 3 + threadIdx.x] = sm[threadIdx.x][0];
+}
+
+static inline int grid1(long long work)
+{
+    long long g = (work + 255) / 256;
+    return (int)std::max(1LL, std::min(g, 148LL * 32));
+}
+
+// ---------------------------------------------------------------------------- communicator handle
+struct GridComm {
+    int P = 1, Q = 1, rank = 0, pr = 0, qc = 0, dev = 0;
+    ncclComm_t world = nullptr, row = nullptr, col = nullptr;
+    double timeout_s = 300.0;
+    bool aborted = false;
+};
+
+// Wait for `st` with a host-side limit; on expiry abort the communicators so
+// that every rank's pending collectives end with an error instead of hanging.
+static int watchdog_sync(GridComm* g, cudaStream_t st, const char* what)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaStreamQuery(st);
+        if (e == cudaSuccess) return CHPL_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(e, what, __FILE__, __LINE__);
+        ncclResult_t ae = ncclSuccess;
+        if (g->world) ncclCommGetAsyncError(g->world, &ae);
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (ae != ncclSuccess || el > g->timeout_s) {
+            if (!g->aborted) {
+                if (g->row) ncclCommAbort(g->row);
+                if (g->col) ncclCommAbort(g->col);
+                if (g->world) ncclCommAbort(g->world);
+                g->row = g->col = g->world = nullptr;
+                g->aborted = true;
+            }
+            set_error("%s: %s after %.1f s; communicators aborted", what,
+                      ae != ncclSuccess ? "NCCL asynchronous error" : "timeout", el);
+            return ae != ncclSuccess ? CHPL_ERR_NCCL : CHPL_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+
+// ---------------------------------------------------------------------------- interchange planning
+// Net effect of the swaps (J+i <-> J+piv[i]), i = 0..K-1 in order, as row
+// moves "dst receives the old contents of src", split for process row pr of P:
+// moves inside this process row (local indices lsrc -> ldst), rows it sends
+// (snd, local source rows) and rows it receives (rcv, local destination rows).
+// Moves are listed in increasing destination order on every rank, so the
+// partner's receive list pairs with this rank's send list element by element.
+static void plan_exchange(int64_t J, int64_t K, const int64_t* piv, int64_t NB, int P, int pr, std::vector<int>& lsrc,
+                          std::vector<int>& ldst, std::vector<int>& snd, std::vector<int>& rcv)
+{
+    std::map<int64_t, int64_t> occ;  // position -> original row now there
+    auto get = [&](int64_t p) { auto it = occ.find(p); return it == occ.end() ? p : it->second; };
+    for (int64_t i = 0; i < K; ++i) {
+        const int64_t a = J + i, b = J + piv[i];
+        if (a == b) continue;
+        const int64_t va = get(a), vb = get(b);
+        occ[a] = vb;
+        occ[b] = va;
+    }
+    auto owner = [&](int64_t gr) { return (int)((gr / NB) % P); };
+    auto local = [&](int64_t gr) { return (int)((gr / NB / P) * NB + gr % NB); };
+    lsrc.clear(); ldst.clear(); snd.clear(); rcv.clear();
+    for (auto& kv : occ) {
+        const int64_t dst = kv.first, src = kv.second;
+        if (dst == src) continue;
+        const int od = owner(dst), os = owner(src);
+        if (od == pr && os == pr) { ldst.push_back(local(dst)); lsrc.push_back(local(src)); }
+        else if (os == pr) snd.push_back(local(src));
+        else if (od == pr) rcv.push_back(local(dst));
+    }
+}
+
+// ---------------------------------------------------------------------------- emulated GEMM helper
+struct Emu {
+    int L = 11;
+    const oz2::Moduli* M = nullptr;
+    void* work = nullptr;   // B part + scratch + split temporaries
+    int64_t chunk = 32768;
+    int64_t launches = 0;
+    double ops = 0.0, flops = 0.0, kernel_s = 0.0;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+
+    // C (m x n) = alpha * A (m x k) * B (k x n) + beta * C; residues of A in wa
+    // (computed here when split_a).  C may alias B when beta == 0.
+    int run(cudaStream_t st, void* wa, bool split_a, int64_t m, int64_t n, int64_t k, const double* A, int64_t lda,
+            const double* B, int64_t ldb, double* C, int64_t ldc, double alpha, double beta)
+    {
+        if (m <= 0 || n <= 0 || k <= 0) return CHPL_OK;
+        for (int64_t c = 0; c < n;) {
+            int64_t w = std::min(chunk, n - c);
+            if (n - c - w > 0 && n - c - w < 1024) w = n - c;
+            const oz2::Layout y = oz2::layout((size_t)m, (size_t)w, (size_t)k, L, true, false);
+            uint8_t* pa = static_cast<uint8_t*>(wa);
+            uint8_t* pb = static_cast<uint8_t*>(work) + y.b_off;
+            int32_t* shA = reinterpret_cast<int32_t*>(pa + y.a_shift);
+            int8_t* resA = reinterpret_cast<int8_t*>(pa + y.a_res);
+            int32_t* shB = reinterpret_cast<int32_t*>(pb + y.b_shift);
+            int8_t* resB = reinterpret_cast<int8_t*>(pb + y.b_res);
+            void* tmp = static_cast<uint8_t*>(work) + y.tmp_off;
+            if (split_a && c == 0) {
+                CHPL_TRY(oz2::split(st, false, A, (size_t)lda, (size_t)m, (size_t)k, L, M->alpha, resA, y.mPad, y.kPad, shA, tmp));
+                launches += 4;
+            }
+            CHPL_TRY(oz2::split(st, true, B + c * ldb, (size_t)ldb, (size_t)w, (size_t)k, L, M->beta, resB, y.nPad, y.kPad,
+                                shB, tmp));
+            cudaEvent_t e0, e1;
+            cudaEventCreate(&e0);
+            cudaEventCreate(&e1);
+            cudaEventRecord(e0, st);
+            CHPL_TRY(oz2::gemm_launch(st, 0, (size_t)m, (size_t)w, y.kPad, L, resA, y.mPad, resB, y.nPad, shA, shB, alpha,
+                                      beta, C + c * ldc, (size_t)ldc, nullptr, 0,
+                                      reinterpret_cast<int8_t*>(static_cast<uint8_t*>(work) + y.scratch_off), y.grid_max));
+            cudaEventRecord(e1, st);
+            ev.push_back({e0, e1});
+            launches += 2;
+            ops += 2.0 * (double)m * (double)w * (double)y.kPad * L;
+            flops += 2.0 * (double)m * (double)w * (double)k;
+            c += w;
+        }
+        return CHPL_OK;
+    }
+
+    void collect()
+    {
+        for (auto& p : ev) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, p.first, p.second) == cudaSuccess) kernel_s += ms * 1e-3;
+            cudaEventDestroy(p.first);
+            cudaEventDestroy(p.second);
+        }
+        ev.clear();
+    }
+};
+
+// ---------------------------------------------------------------------------- grid solver
+struct GridSolver {
+    GridComm* g = nullptr;
+    chpl_hpl_config cfg{};
+    int64_t N = 0, NB = 0, NBp = 0, mloc = 0, nloc = 0, lda = 0, nblk = 0;
+    cudaStream_t st = nullptr;
+    cublasHandle_t hb = nullptr;
+    double* A = nullptr;
+    double* arena = nullptr;       // gathered panel + pack buffer (factor phase), then W + U12 buffers
+    size_t arena_elems = 0;
+    void* wres = nullptr;          // residues of W (A part)
+    void* win = nullptr;           // residues of inner-update L21 (A part)
+    double* linv = nullptr;        // inv(L11)
+    void* wlinv = nullptr;         // its residues
+    double* xch = nullptr;         // exchange buffers (3 x 2 NB x kXchCols)
+    int* dlist = nullptr;          // device copies of exchange row lists
+    int64_t* piv = nullptr;        // pivots of the current block column (relative to J)
+    int* info = nullptr;
+    void* pwork = nullptr;
+    void* plan = nullptr;
+    double* x = nullptr;           // solution (N)
+    double* tsum = nullptr;        // back-substitution partial sums (mloc)
+    double* vbuf = nullptr;        // NB
+    Emu emu;
+    int64_t n_launch = 0;
+    double phase[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    static constexpr int64_t kXchCols = 4096;
+
+    int owner_row(int64_t gr) const { return (int)((gr / NB) % g->P); }
+    int64_t local_row(int64_t gr) const { return (gr / NB / g->P) * NB + gr % NB; }
+    int root_of(int p, int q) const { return g->P * q + p; }
+
+    int init(GridComm* gc, const chpl_hpl_config& c)
+    {
+        g = gc;
+        cfg = c;
+        N = c.N;
+        NB = std::min<int64_t>(c.NB, N);
+        NBp = std::min<int64_t>(NB, c.agg > 0 ? std::max<int64_t>(1, NB / c.agg) : 1024);
+        nblk = (N + NB - 1) / NB;
+        mloc = local_extent(N, NB, g->P, g->pr);
+        nloc = local_extent(N + 1, NB, g->Q, g->qc);
+        lda = (int64_t)round_up((size_t)std::max<int64_t>(mloc, 1), 32);
+        int lo = 0, hi = 0;
+        CHPL_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        CHPL_CUDA(cudaStreamCreateWithPriority(&st, cudaStreamNonBlocking, hi));
+        CHPL_CUBLAS_G(cublasCreate(&hb));
+        CHPL_CUBLAS_G(cublasSetStream(hb, st));
+        const unsigned L = (unsigned)cfg.moduli;
+        emu.L = (int)L;
+        emu.M = oz2::moduli(cfg.moduli);
+        if (!emu.M) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
+        emu.chunk = cfg.chunk > 0 ? cfg.chunk : 32768;
+        // sizes
+        const size_t bytesA = (size_t)lda * (size_t)nloc * 8;
+        const size_t g_elems = (g->P > 1) ? (size_t)N * NB + (size_t)(mloc + NB) * NB : 0;  // gathered panel + pack
+        const size_t wu_elems = (size_t)mloc * NB + (size_t)NB * nloc;                       // W + U12
+        arena_elems = std::max(g_elems, wu_elems);
+        size_t tot = 0, wa = 0, wb = 0, tin = 0, ain = 0, bin = 0, tl = 0, al = 0, bl = 0;
+        const int64_t mmax = std::max<int64_t>(std::max(mloc, (g->P > 1) ? N : mloc), NB);
+        CHPL_TRY(chpl_oz2_worksize((size_t)mloc, (size_t)std::min<int64_t>(emu.chunk + 1024, std::max<int64_t>(nloc, 1)),
+                                   (size_t)NB, L, 1, 0, &tot, &wa, &wb));
+        CHPL_TRY(chpl_oz2_worksize((size_t)mmax, (size_t)NB, (size_t)NBp, L, 1, 0, &tin, &ain, &bin));
+        CHPL_TRY(chpl_oz2_worksize((size_t)NB, 256, (size_t)NB, L, 1, 0, &tl, &al, &bl));
+        const size_t work_bytes = std::max(tot - wa, tin - ain);
+        const size_t xch_bytes = (size_t)3 * 2 * NB * kXchCols * 8;
+        size_t freeB = 0, totB = 0;
+        CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
+        const size_t need = bytesA + arena_elems * 8 + wa + ain + (size_t)NB * NB * 8 + al + xch_bytes + work_bytes +
+                            panel_work_bytes(mmax, NBp) + (size_t)N * 8 * 2 + (size_t)mloc * 8 + ((size_t)768 << 20);
+        if (cfg.verbose && g->rank == 0)
+            std::printf("GRID MEM PLAN (rank 0): local %lld x %lld, matrix %.2f GiB, total %.2f GiB of %.2f GiB free\n",
+                        (long long)mloc, (long long)nloc, bytesA / 1073741824.0, need / 1073741824.0, freeB / 1073741824.0);
+        if (need > freeB) {
+            set_error("grid memory plan: need %.2f GiB, %.2f GiB free (reduce N)", need / 1073741824.0, freeB / 1073741824.0);
+            return CHPL_ERR_WORKSPACE;
+        }
+        CHPL_CUDA(cudaMalloc((void**)&A, std::max<size_t>(bytesA, 8)));
+        CHPL_CUDA(cudaMalloc((void**)&arena, std::max<size_t>(arena_elems, 1) * 8));
+        CHPL_CUDA(cudaMalloc(&wres, wa));
+        CHPL_CUDA(cudaMalloc(&win, ain));
+        CHPL_CUDA(cudaMalloc((void**)&linv, (size_t)NB * NB * 8));
+        CHPL_CUDA(cudaMalloc(&wlinv, al));
+        CHPL_CUDA(cudaMalloc((void**)&xch, xch_bytes));
+        CHPL_CUDA(cudaMalloc((void**)&dlist, (size_t)4 * 2 * NB * sizeof(int)));
+        CHPL_CUDA(cudaMalloc((void**)&piv, (size_t)NB * sizeof(int64_t)));
+        CHPL_CUDA(cudaMalloc((void**)&info, 16 * sizeof(int)));
+        CHPL_CUDA(cudaMemset(info, 0, 16 * sizeof(int)));
+        CHPL_CUDA(cudaMalloc(&pwork, panel_work_bytes(mmax, NBp)));
+        CHPL_CUDA(cudaMalloc(&plan, laswp_work_bytes(NBp)));
+        CHPL_CUDA(cudaMalloc(&emu.work, work_bytes));
+        CHPL_CUDA(cudaMalloc((void**)&x, (size_t)N * 8));
+        CHPL_CUDA(cudaMalloc((void**)&tsum, (size_t)std::max<int64_t>(mloc, 1) * 8));
+        CHPL_CUDA(cudaMalloc((void**)&vbuf, (size_t)NB * 8 * 2));
+        return CHPL_OK;
+    }
+
+    void destroy()
+    {
+        emu.collect();
+        void* ps[] = {A, arena, wres, win, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf};
+        for (void* p : ps)
+            if (p) cudaFree(p);
+        if (hb) cublasDestroy(hb);
+        if (st) cudaStreamDestroy(st);
+    }
+
+    // exact partial pivoting LU of an m x K panel (ld) in place, internal
+    // panels of width NBp; piv[i] relative to the panel top
+    int factor_panel(double* Pm, int64_t ldp, int64_t m, int64_t K)
+    {
+        const double one = 1.0;
+        for (int64_t jp = 0; jp < K; jp += NBp) {
+            const int64_t nb = std::min(NBp, K - jp);
+            CHPL_TRY(panel_getrf(st, m - jp, nb, Pm + jp + jp * ldp, (size_t)ldp, piv + jp, jp, info, pwork));
+            CHPL_TRY(laswp_plan(st, piv, jp, jp + nb, plan));
+            CHPL_TRY(laswp_apply(st, Pm, (size_t)ldp, 0, jp, nb, plan));
+            CHPL_TRY(laswp_apply(st, Pm, (size_t)ldp, jp + nb, K - jp - nb, nb, plan));
+            n_launch += 4 + 2 * ((nb + 15) / 16) * 2;
+            const int64_t nr = K - jp - nb;
+            if (nr > 0) {
+                CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, nb,
+                                             nr, &one, Pm + jp + jp * ldp, ldp, Pm + jp + (jp + nb) * ldp, ldp));
+                CHPL_TRY(emu.run(st, win, true, m - jp - nb, nr, nb, Pm + (jp + nb) + jp * ldp, ldp, Pm + jp + (jp + nb) * ldp,
+                                 ldp, Pm + (jp + nb) + (jp + nb) * ldp, ldp, -1.0, 1.0));
+            }
+        }
+        return CHPL_OK;
+    }
+
+    int rows_gather(double* dst, int64_t ldd, const double* Ab, const int* rows, int n, int64_t ncols)
+    {
+        if (n <= 0 || ncols <= 0) return CHPL_OK;
+        rows_gather_kernel<<<grid1((long long)n * ncols), 256, 0, st>>>(dst, ldd, Ab, lda, rows, n, ncols);
+        ++n_launch;
+        CHPL_CUDA(cudaGetLastError());
+        return CHPL_OK;
+    }
+
+    int rows_scatter(double* Ab, const double* src, int64_t lds, const int* rows, int n, int64_t ncols)
+    {
+        if (n <= 0 || ncols <= 0) return CHPL_OK;
+        rows_scatter_kernel<<<grid1((long long)n * ncols), 256, 0, st>>>(Ab, lda, src, lds, rows, n, ncols);
+        ++n_launch;
+        CHPL_CUDA(cudaGetLastError());
+        return CHPL_OK;
+    }
+
+    int block_step(int64_t s)
+    {
+        const int P = g->P, pr = g->pr, qc = g->qc;
+        const int64_t J = s * NB, K = std::min(NB, N - J);
+        const int ps = (int)(s % P), qs = (int)(s % g->Q);
+        const int64_t lrb = local_extent(J, NB, P, pr);            // my first active local row
+        const int64_t mact = mloc - lrb;
+        const int64_t lc = local_extent(J, NB, g->Q, qc);          // local column of global J (on qs)
+        const int64_t tc0 = local_extent(J + K, NB, g->Q, qc);     // first trailing local column
+        const int64_t ntr = nloc - tc0;
+        const int64_t lrw = local_extent(J + K, NB, P, pr);        // first local row below the diagonal block
+        const int64_t mW = mloc - lrw;
+        const double one = 1.0;
+        auto t0 = std::chrono::steady_clock::now();
+
+        // ---- 1. factor the block column on its diagonal owner ----
+        if (qc == qs) {
+            if (P == 1) {
+                CHPL_TRY(factor_panel(A + lrb + lc * lda, lda, N - J, K));
+            } else {
+                const int partner = 1 - pr;
+                const int64_t lrb_o = local_extent(J, NB, P, partner), mact_o = local_extent(N, NB, P, partner) - lrb_o;
+                double* G = arena;                          // (N - J) x K, ld N - J
+                double* Sb = arena + (size_t)N * NB;        // pack buffer, ld = rows of the packing rank
+                const int64_t mg = N - J;
+                if (pr == ps) {
+                    CHPL_NCCL(ncclRecv(Sb, (size_t)mact_o * K, ncclDouble, partner, g->col, st));
+                    panel_shuffle_kernel<<<grid1(mg * K), 256, 0, st>>>(G, mg, mg, K, J, NB, P, pr, A + lrb + lc * lda, lda,
+                                                                       lrb, Sb, mact_o, lrb_o, 0);
+                    CHPL_TRY(factor_panel(G, mg, mg, K));
+                    panel_shuffle_kernel<<<grid1(mg * K), 256, 0, st>>>(G, mg, mg, K, J, NB, P, pr, A + lrb + lc * lda, lda,
+                                                                       lrb, Sb, mact_o, lrb_o, 1);
+                    n_launch += 2;
+                    CHPL_NCCL(ncclSend(Sb, (size_t)mact_o * K, ncclDouble, partner, g->col, st));
+                } else {
+                    CHPL_CUDA(cudaMemcpy2DAsync(Sb, (size_t)mact * 8, A + lrb + lc * lda, (size_t)lda * 8, (size_t)mact * 8,
+                                                (size_t)K, cudaMemcpyDeviceToDevice, st));
+                    CHPL_NCCL(ncclSend(Sb, (size_t)mact * K, ncclDouble, ps, g->col, st));
+                    CHPL_NCCL(ncclRecv(Sb, (size_t)mact * K, ncclDouble, ps, g->col, st));
+                    CHPL_CUDA(cudaMemcpy2DAsync(A + lrb + lc * lda, (size_t)lda * 8, Sb, (size_t)mact * 8, (size_t)mact * 8,
+                                                (size_t)K, cudaMemcpyDeviceToDevice, st));
+                }
+            }
+        }
+        // ---- 2. pivots to everyone; inv(L11) along the diagonal process row ----
+        CHPL_NCCL(ncclBroadcast(piv, piv, (size_t)K, ncclInt64, root_of(ps, qs), g->world, st));
+        if (pr == ps) {
+            if (qc == qs) {
+                CHPL_TRY(identity(st, linv, K));
+                CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K, K,
+                                             &one, A + lrb + lc * lda, lda, linv, K));
+                ++n_launch;
+            }
+            if (g->Q > 1) CHPL_NCCL(ncclBroadcast(linv, linv, (size_t)K * K, ncclDouble, qs, g->row, st));
+        }
+        // W = rows below the diagonal block of the block column, along process rows
+        double* W = arena;
+        double* U = arena + (size_t)mloc * NB;
+        if (qc == qs && mW > 0)
+            CHPL_CUDA(cudaMemcpy2DAsync(W, (size_t)mW * 8, A + lrw + lc * lda, (size_t)lda * 8, (size_t)mW * 8, (size_t)K,
+                                        cudaMemcpyDeviceToDevice, st));
+        if (g->Q > 1 && mW > 0) CHPL_NCCL(ncclBroadcast(W, W, (size_t)mW * K, ncclDouble, qs, g->row, st));
+        // host copy of the pivots to plan the interchanges
+        std::vector<int64_t> hp((size_t)K);
+        CHPL_CUDA(cudaMemcpyAsync(hp.data(), piv, (size_t)K * 8, cudaMemcpyDeviceToHost, st));
+        CHPL_TRY(watchdog_sync(g, st, "factor/broadcast"));
+        phase[0] += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        t0 = std::chrono::steady_clock::now();
+
+        // ---- 3. interchanges of the trailing columns ----
+        std::vector<int> lsrc, ldst, snd, rcv;
+        plan_exchange(J, K, hp.data(), NB, P, pr, lsrc, ldst, snd, rcv);
+        if (ntr > 0 && (!ldst.empty() || !snd.empty() || !rcv.empty())) {
+            int* dl = dlist;
+            std::vector<int> all;
+            all.insert(all.end(), lsrc.begin(), lsrc.end());
+            all.insert(all.end(), ldst.begin(), ldst.end());
+            all.insert(all.end(), snd.begin(), snd.end());
+            all.insert(all.end(), rcv.begin(), rcv.end());
+            CHPL_CUDA(cudaMemcpyAsync(dl, all.data(), all.size() * sizeof(int), cudaMemcpyHostToDevice, st));
+            const int nl = (int)lsrc.size(), ns = (int)snd.size(), nr = (int)rcv.size();
+            const int* d_lsrc = dl;
+            const int* d_ldst = dl + nl;
+            const int* d_snd = dl + 2 * nl;
+            const int* d_rcv = dl + 2 * nl + ns;
+            double* Tb = xch;
+            double* Sb2 = xch + (size_t)2 * NB * kXchCols;
+            double* Rb = xch + (size_t)4 * NB * kXchCols;
+            for (int64_t c0 = tc0; c0 < nloc; c0 += kXchCols) {
+                const int64_t nc = std::min(kXchCols, nloc - c0);
+                double* Ab = A + c0 * lda;
+                CHPL_TRY(rows_gather(Sb2, std::max(ns, 1), Ab, d_snd, ns, nc));
+                CHPL_TRY(rows_gather(Tb, std::max(nl, 1), Ab, d_lsrc, nl, nc));
+                if (ns > 0 || nr > 0) {
+                    CHPL_NCCL(ncclGroupStart());
+                    if (ns > 0) CHPL_NCCL(ncclSend(Sb2, (size_t)ns * nc, ncclDouble, 1 - pr, g->col, st));
+                    if (nr > 0) CHPL_NCCL(ncclRecv(Rb, (size_t)nr * nc, ncclDouble, 1 - pr, g->col, st));
+                    CHPL_NCCL(ncclGroupEnd());
+                }
+                CHPL_TRY(rows_scatter(Ab, Tb, std::max(nl, 1), d_ldst, nl, nc));
+                CHPL_TRY(rows_scatter(Ab, Rb, std::max(nr, 1), d_rcv, nr, nc));
+            }
+        }
+        // ---- 4. U12 on the diagonal process row, down the process columns ----
+        if (ntr > 0) {
+            if (pr == ps) {
+                CHPL_TRY(emu.run(st, wlinv, true, K, ntr, K, linv, K, A + lrb + tc0 * lda, lda, A + lrb + tc0 * lda, lda, 1.0,
+                                 0.0));
+                if (P > 1)
+                    CHPL_CUDA(cudaMemcpy2DAsync(U, (size_t)K * 8, A + lrb + tc0 * lda, (size_t)lda * 8, (size_t)K * 8,
+                                                (size_t)ntr, cudaMemcpyDeviceToDevice, st));
+            }
+            if (P > 1) CHPL_NCCL(ncclBroadcast(U, U, (size_t)K * ntr, ncclDouble, ps, g->col, st));
+            // ---- 5. trailing update ----
+            if (mW > 0) {
+                const double* Bp = (P > 1) ? U : A + lrb + tc0 * lda;
+                const int64_t ldb = (P > 1) ? K : lda;
+                CHPL_TRY(emu.run(st, wres, true, mW, ntr, K, W, mW, Bp, ldb, A + lrw + tc0 * lda, lda, -1.0, 1.0));
+            }
+        }
+        CHPL_TRY(watchdog_sync(g, st, "update"));
+        phase[3] += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        return CHPL_OK;
+    }
+
+    // distributed back substitution U x = b' (b' in global column N)
+    int back_solve()
+    {
+        const int P = g->P, Q = g->Q, pr = g->pr, qc = g->qc;
+        const int qN = (int)((N / NB) % Q);
+        const int64_t lcN = local_extent(N, NB, Q, qN);
+        CHPL_CUDA(cudaMemsetAsync(tsum, 0, (size_t)std::max<int64_t>(mloc, 1) * 8, st));
+        CHPL_CUDA(cudaMemsetAsync(x, 0, (size_t)N * 8, st));
+        const double one = 1.0;
+        for (int64_t j = nblk - 1; j >= 0; --j) {
+            const int64_t J = j * NB, jb = std::min(NB, N - J);
+            const int pj = (int)(j % P), qj = (int)(j % Q);
+            const int64_t lrj = local_extent(J, NB, P, pj);
+            double* v = vbuf;
+            if (pr == pj) {
+                axpby_rows_kernel<<<(unsigned)((jb + 255) / 256), 256, 0, st>>>(v, A + lrj + lcN * lda, tsum + lrj, (int)jb,
+                                                                              qc == qN ? 1 : 0);
+                ++n_launch;
+                if (Q > 1) CHPL_NCCL(ncclReduce(v, v, (size_t)jb, ncclDouble, ncclSum, qj, g->row, st));
+                if (qc == qj) {
+                    const int64_t lcj = local_extent(J, NB, Q, qj);
+                    CHPL_CUBLAS_G(cublasDtrsv_64(hb, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N, CUBLAS_DIAG_NON_UNIT, jb,
+                                                 A + lrj + lcj * lda, lda, v, 1));
+                }
+            }
+            if (qc == qj) {
+                if (P > 1) CHPL_NCCL(ncclBroadcast(v, v, (size_t)jb, ncclDouble, pj, g->col, st));
+                const int64_t lcj = local_extent(J, NB, Q, qj);
+                const int64_t rows_above = local_extent(J, NB, P, pr);
+                if (rows_above > 0)
+                    CHPL_CUBLAS_G(cublasDgemv_64(hb, CUBLAS_OP_N, rows_above, jb, &one, A + lcj * lda, lda, v, 1, &one, tsum, 1));
+                if (pr == 0) CHPL_CUDA(cudaMemcpyAsync(x + J, v, (size_t)jb * 8, cudaMemcpyDeviceToDevice, st));
+            }
+        }
+        if (g->P * g->Q > 1) CHPL_NCCL(ncclAllReduce(x, x, (size_t)N, ncclDouble, ncclSum, g->world, st));
+        return watchdog_sync(g, st, "back substitution");
+    }
+
+    int residual(double* resid)
+    {
+        const long long nbk = (mloc + 255) / 256;
+        double* part = nullptr;
+        double* axrs = nullptr;
+        double* out = nullptr;
+        CHPL_CUDA(cudaMallocAsync((void**)&part, (size_t)kGridResChunks * 2 * std::max<int64_t>(mloc, 1) * 8, st));
+        CHPL_CUDA(cudaMallocAsync((void**)&axrs, (size_t)2 * std::max<int64_t>(mloc, 1) * 8, st));
+        CHPL_CUDA(cudaMallocAsync((void**)&out, (size_t)std::max(nbk, 1LL) * 3 * 8 + 64, st));
+        if (mloc > 0) {
+            grid_resid_partial_kernel<<<dim3((unsigned)nbk, kGridResChunks), 256, 0, st>>>(
+                N, NB, g->P, g->Q, g->pr, g->qc, mloc, nloc, cfg.seed, x, part);
+            grid_resid_sum_kernel<<<(unsigned)nbk, 256, 0, st>>>(mloc, part, axrs);
+        }
+        if (g->Q > 1 && mloc > 0) CHPL_NCCL(ncclAllReduce(axrs, axrs, (size_t)2 * mloc, ncclDouble, ncclSum, g->row, st));
+        if (mloc > 0) grid_resid_max_kernel<<<(unsigned)nbk, 256, 0, st>>>(N, NB, g->P, g->pr, mloc, cfg.seed, axrs, out);
+        std::vector<double> h((size_t)std::max(nbk, 1LL) * 3, 0.0);
+        if (mloc > 0) CHPL_CUDA(cudaMemcpyAsync(h.data(), out, (size_t)nbk * 3 * 8, cudaMemcpyDeviceToHost, st));
+        CHPL_TRY(watchdog_sync(g, st, "residual"));
+        double loc[4] = {0, 0, 0, 0};
+        for (long long b = 0; b < nbk; ++b)
+            for (int q = 0; q < 3; ++q) loc[q] = std::max(loc[q], h[(size_t)b * 3 + q]);
+        // ||x||_oo (x is complete on every rank)
+        std::vector<double> hx((size_t)N);
+        CHPL_CUDA(cudaMemcpy(hx.data(), x, (size_t)N * 8, cudaMemcpyDeviceToHost));
+        for (double v : hx) loc[3] = std::max(loc[3], std::fabs(v));
+        double* dm = out;
+        CHPL_CUDA(cudaMemcpyAsync(dm, loc, 4 * 8, cudaMemcpyHostToDevice, st));
+        if (g->P * g->Q > 1) CHPL_NCCL(ncclAllReduce(dm, dm, 4, ncclDouble, ncclMax, g->world, st));
+        double gl[4];
+        CHPL_CUDA(cudaMemcpyAsync(gl, dm, 4 * 8, cudaMemcpyDeviceToHost, st));
+        CHPL_TRY(watchdog_sync(g, st, "residual reduce"));
+        cudaFreeAsync(part, st);
+        cudaFreeAsync(axrs, st);
+        cudaFreeAsync(out, st);
+        const double eps = std::ldexp(1.0, -53);
+        *resid = gl[0] / (eps * (gl[1] * gl[3] + gl[2]) * (double)N);
+        return CHPL_OK;
+    }
+};
+
+static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)
+{
+    if (!g || !cfg || !res) { set_error("grid_run: NULL argument"); return CHPL_ERR_INVALID; }
+    std::memset(res, 0, sizeof(*res));
+    if (g->aborted) { set_error("communicators were aborted"); return CHPL_ERR_NCCL; }
+    if (cfg->P != g->P || cfg->Q != g->Q) { set_error("config grid %dx%d != communicator grid %dx%d", cfg->P, cfg->Q, g->P, g->Q); return CHPL_ERR_INVALID; }
+    if (g->P > 2) { set_error("process grids with P > 2 are not supported (P = 1 or 2)"); return CHPL_ERR_UNSUPPORTED; }
+    if (cfg->N <= 0 || cfg->NB <= 0 || cfg->NB > 16384) { set_error("bad N/NB"); return CHPL_ERR_INVALID; }
+    if (!cfg->emulate) { set_error("the grid driver runs the emulated update only (CHPL2D_G8=1)"); return CHPL_ERR_UNSUPPORTED; }
+    GridSolver s;
+    int rc = s.init(g, *cfg);
+    auto finish = [&](int code) { s.destroy(); return code; };
+    if (rc != CHPL_OK) return finish(rc);
+    // generation (not timed)
+    const int P = g->P, Q = g->Q;
+    if (s.mloc > 0 && s.nloc > 0) CHPL_TRY(chpl_matgen_cyclic(s.st, s.A, (size_t)s.lda, s.N, s.NB, P, Q, g->pr, g->qc, cfg->seed));
+    rc = watchdog_sync(g, s.st, "matgen");
+    if (rc != CHPL_OK) return finish(rc);
+    cudaEvent_t t0, t1;
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(t0, s.st);
+    for (int64_t b = 0; b < s.nblk && rc == CHPL_OK; ++b) rc = s.block_step(b);
+    if (rc == CHPL_OK) rc = s.back_solve();
+    if (rc != CHPL_OK) return finish(rc);
+    cudaEventRecord(t1, s.st);
+    cudaEventSynchronize(t1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, t0, t1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    int hinfo = 0;
+    cudaMemcpy(&hinfo, s.info, sizeof(int), cudaMemcpyDeviceToHost);
+    int perr = 0;
+    panel_status(s.pwork, &perr);
+    int dstat = 0;
+    oz2::read_clear_status(&dstat);
+    if (perr || dstat) { set_error("device-side timeout (panel %d, update %d)", perr, dstat); return finish(CHPL_ERR_TIMEOUT); }
+    res->time_s = ms * 1e-3;
+    const double dN = (double)s.N;
+    res->tflops = ((2.0 / 3.0) * dN * dN * dN + 2.0 * dN * dN) / res->time_s / 1e12;
+    rc = s.residual(&res->resid);
+    if (rc != CHPL_OK) return finish(rc);
+    res->passed = hinfo == 0 && std::isfinite(res->resid) && res->resid < cfg->threshold;
+    s.emu.collect();
+    res->phase_s[0] = s.phase[0];
+    res->phase_s[4] = s.phase[3];
+    res->gemm_launches = (int64_t)0;
+    res->gemm_kernel_s = s.emu.kernel_s;
+    res->gemm_int8_ops = s.emu.ops;
+    res->gemm_fp64eq_flops = s.emu.flops;
+    res->n_launches = s.n_launch + s.emu.launches;
+    res->n_emulated = s.emu.launches / 2;
+    res->gemm_launches = s.emu.launches / 2;
+    if (x_out) {
+        cudaError_t e = cudaMemcpy(x_out, s.x, (size_t)s.N * 8, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return finish(cuda_fail(e, "x readback", __FILE__, __LINE__));
+    }
+    if (hinfo != 0) { set_error("exact zero pivot (info %d)", hinfo); return finish(CHPL_ERR_SINGULAR); }
+    return finish(CHPL_OK);
+}
+
+}  // namespace chpl
+
+using namespace chpl;
+
+extern "C" int chpl_grid_unique_id(unsigned char* id, size_t len)
+{
+    if (!id || len < sizeof(ncclUniqueId)) { set_error("unique id buffer must hold %zu bytes", sizeof(ncclUniqueId)); return CHPL_ERR_INVALID; }
+    ncclUniqueId u;
+    CHPL_NCCL(ncclGetUniqueId(&u));
+    std::memcpy(id, &u, sizeof(u));
+    return CHPL_OK;
+}
+
+extern "C" int chpl_grid_create(int P, int Q, int rank, const unsigned char* id, size_t len, double timeout_s,
+                                void** grid)
+{
+    if (!grid || !id || len < sizeof(ncclUniqueId) || P < 1 || Q < 1 || rank < 0 || rank >= P * Q) {
+        set_error("chpl_grid_create: bad arguments");
+        return CHPL_ERR_INVALID;
+    }
+    GridComm* g = new GridComm();
+    g->P = P;
+    g->Q = Q;
+    g->rank = rank;
+    g->pr = rank % P;
+    g->qc = rank / P;
+    g->timeout_s = timeout_s > 0 ? timeout_s : 300.0;
+    CHPL_CUDA(cudaGetDevice(&g->dev));
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof(u));
+    ncclResult_t r = ncclCommInitRank(&g->world, P * Q, u, rank);
+    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->pr, g->qc, &g->row, nullptr);   // same process row
+    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->qc, g->pr, &g->col, nullptr);   // same process column
+    if (r != ncclSuccess) {
+        set_error("NCCL communicator setup failed: %s", ncclGetErrorString(r));
+        delete g;
+        return CHPL_ERR_NCCL;
+    }
+    *grid = g;
+    return CHPL_OK;
+}
+
+extern "C" int chpl_grid_run(void* grid, const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)
+{
+    return grid_run(static_cast<GridComm*>(grid), cfg, res, x_out);
+}
+
+extern "C" int chpl_grid_destroy(void* grid)
+{
+    GridComm* g = static_cast<GridComm*>(grid);
+    if (!g) return CHPL_OK;
+    if (!g->aborted) {
+        if (g->row) ncclCommDestroy(g->row);
+        if (g->col) ncclCommDestroy(g->col);
+        if (g->world) ncclCommDestroy(g->world);
+    }
+    delete g;
+    return CHPL_OK;
+}
+
+extern "C" int chpl_grid_plan_exchange(int64_t J, int64_t K, const int64_t* piv, int64_t NB, int P, int pr, int* lsrc,
+                                       int* ldst, int* nl, int* snd, int* ns, int* rcv, int* nr)
+{
+    if (!piv || K < 0 || NB <= 0 || P < 1 || pr < 0 || pr >= P || !nl || !ns || !nr) {
+        set_error("chpl_grid_plan_exchange: bad arguments");
+        return CHPL_ERR_INVALID;
+    }
+    for (int64_t i = 0; i < K; ++i)
+        if (piv[i] < i) { set_error("pivot %lld < position %lld", (long long)piv[i], (long long)i); return CHPL_ERR_INVALID; }
+    std::vector<int> a, b, c, d;
+    plan_exchange(J, K, piv, NB, P, pr, a, b, c, d);
+    *nl = (int)a.size();
+    *ns = (int)c.size();
+    *nr = (int)d.size();
+    if (lsrc) std::copy(a.begin(), a.end(), lsrc);
+    if (ldst) std::copy(b.begin(), b.end(), ldst);
+    if (snd) std::copy(c.begin(), c.end(), snd);
+    if (rcv) std::copy(d.begin(), d.end(), rcv);
+    return CHPL_OK;
+}

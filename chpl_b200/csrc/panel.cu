@@ -288,8 +288,9 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
 // ipiv entries of this node are relative to the node's top row + base_row
 int rec(PanelCtx& c, double* A, int64_t lda, int64_t m, int64_t n, int64_t* ipiv, int64_t base_row, int info_off)
 {
-    // base width: 32 columns when the rows fit on chip, else 16
-    const int bw = ((m + c.h->grid - 1) / c.h->grid) * 32 * 8 <= kSmemBytes ? 32 : 16;
+    // base width: the widest of 32 / 16 / 8 columns whose rows fit on chip
+    const int64_t rows_sm = (m + c.h->grid - 1) / c.h->grid;
+    const int bw = rows_sm * 32 * 8 <= kSmemBytes ? 32 : rows_sm * 16 * 8 <= kSmemBytes ? 16 : 8;
     if (n <= bw) return base_block(c, A, lda, m, (int)n, ipiv, base_row, info_off);
     int64_t n1 = ((n / 2) + bw - 1) / bw * bw;
     const int64_t n2 = n - n1;

@@ -231,6 +231,34 @@ void chpl_hpl_default_config(chpl_hpl_config *cfg);
  */
 int chpl_hpl_run(const chpl_hpl_config *cfg, chpl_hpl_result *res, double *x_out);
 
+/* ------------------------------------------------------------------------ */
+/* P x Q process grid (one process per GPU, NCCL over NVLink)                */
+/* ------------------------------------------------------------------------ */
+
+/* NCCL unique id for the grid (rank 0 creates it and shares the bytes with
+ * the other ranks by any host channel).  Replaces the MPI_Bcast of NCCL ids
+ * of src/chpl_p2.cu:552-568.  len >= 128. */
+int chpl_grid_unique_id(unsigned char *id, size_t len);
+/* World, process-row and process-column communicators of rank `rank` of a
+ * P x Q grid (pr = rank % P, qc = rank / P, src/chpl_p2.cu:528), on the
+ * current device.  timeout_s bounds every host-side wait; past it the
+ * communicators are aborted and calls return CHPL_ERR_TIMEOUT.
+ * Replaces the MPI/NCCL bootstrap of src/chpl_p2.cu:520-568. */
+int chpl_grid_create(int P, int Q, int rank, const unsigned char *id, size_t len, double timeout_s, void **grid);
+/* One HPL solve on the grid (all ranks call it): block-cyclic generation,
+ * factorization, distributed back substitution and residual.  res is the
+ * same on every rank except time_s (this rank's device time).  x_out (host,
+ * N) may be NULL.  Replaces main() of src/chpl_p2.cu (lines 518-1953). */
+int chpl_grid_run(void *grid, const chpl_hpl_config *cfg, chpl_hpl_result *res, double *x_out);
+int chpl_grid_destroy(void *grid);
+/* Host-only: the row moves of one block column's interchanges (swaps
+ * J+i <-> J+piv[i], i < K) for process row pr of P: local moves
+ * (lsrc -> ldst), rows sent (snd) and received (rcv) across process rows,
+ * each array >= 2K entries.  The reference builds the same lists on the
+ * device (buildlists_kernel, src/chpl_p2.cu:255-300). */
+int chpl_grid_plan_exchange(int64_t J, int64_t K, const int64_t *piv, int64_t NB, int P, int pr, int *lsrc,
+                            int *ldst, int *nl, int *snd, int *ns, int *rcv, int *nr);
+
 #ifdef __cplusplus
 }
 #endif

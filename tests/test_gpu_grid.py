@@ -1,0 +1,91 @@
+"""GPU tests of the P x Q grid driver (one process per GPU, NCCL).
+
+The 1 x 1 grid runs in this process on one GPU; grids of 2 ranks (1 x 2,
+2 x 1) and 4 ranks (2 x 2) run as spawned processes when the machine has that
+many GPUs (NVLS off, as for every multi-rank test on this pool)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from chpl_b200 import hpl
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, P, Q, N, NB, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from chpl_b200 import grid
+    dist = grid.init_from_env(timeout_s=300)
+    g = grid.Grid(P, Q, timeout_s=120)
+    r = g.run(hpl.Config(N=N, NB=NB, P=P, Q=Q, moduli=12), want_x=True)
+    g.close()
+    out[rank] = (r.passed, r.resid, r.x)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_spawned(P, Q, N, NB):
+    import torch.multiprocessing as mp
+    world = P * Q
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        mp.start_processes(_worker, args=(world, _free_port(), P, Q, N, NB, out), nprocs=world, join=True,
+                           start_method="spawn")
+        return dict(out)
+
+
+def _reference_x(N):
+    S = oracle.hpl_system(N)
+    return np.linalg.solve(S[:, :N], S[:, N])
+
+
+def test_grid_1x1_in_process(cuda):
+    import torch.distributed as dist
+    from chpl_b200 import grid
+    if not dist.is_initialized():
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    g = grid.Grid(1, 1)
+    r = g.run(hpl.Config(N=3000, NB=512, P=1, Q=1, moduli=12, agg=2), want_x=True)
+    g.close()
+    assert r.passed, r.resid
+    assert np.allclose(r.x, _reference_x(3000), rtol=1e-6, atol=1e-8)
+
+
+@pytest.mark.parametrize("grid_shape", [(1, 2), (2, 1)])
+def test_grid_two_ranks(cuda, grid_shape):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    P, Q = grid_shape
+    N, NB = 4000, 256
+    out = _run_spawned(P, Q, N, NB)
+    xs = _reference_x(N)
+    for rank in range(P * Q):
+        passed, resid, x = out[rank]
+        assert passed, resid
+        assert np.allclose(x, xs, rtol=1e-6, atol=1e-8)
+
+
+def test_grid_2x2(cuda):
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    out = _run_spawned(2, 2, 5000, 256)
+    xs = _reference_x(5000)
+    for rank in range(4):
+        passed, resid, x = out[rank]
+        assert passed, resid
+        assert np.allclose(x, xs, rtol=1e-6, atol=1e-8)

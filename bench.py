@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--NB", type=int, default=0)
     ap.add_argument("--moduli", type=int, default=11)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-lookahead", action="store_true")
+    ap.add_argument("--lookahead", action="store_true", help="SM-reserving depth-1 lookahead (default: serial)")
     return ap.parse_args()
 
 
@@ -202,7 +202,7 @@ def run_single(a) -> None:
 
     from chpl_b200 import _lib, hpl
     N, NB = (a.N, a.NB or 1024) if a.N else WORKLOADS[1][:2]
-    cfg = hpl.Config(N=N, NB=NB, moduli=a.moduli, lookahead=not a.no_lookahead)
+    cfg = hpl.Config(N=N, NB=NB, moduli=a.moduli, lookahead=a.lookahead)
     torch.cuda.set_device(0)
     peak_i8 = int8_peak_tops()
     for _ in range(a.warmup):
@@ -241,7 +241,7 @@ def run_single(a) -> None:
         "data": "synthetic (chpl SplitMix64 generator, seed 42)",
         "config": {"workload": f"HPL solve N={N} NB={NB} 1x1 grid, {a.moduli} moduli (BASELINE config 3)"
                    if not a.N else f"HPL solve N={N} NB={NB} 1x1 grid, {a.moduli} moduli",
-                   "N": N, "NB": NB, "grid": "1x1", "moduli": a.moduli, "lookahead": not a.no_lookahead,
+                   "N": N, "NB": NB, "grid": "1x1", "moduli": a.moduli, "lookahead": a.lookahead,
                    "l2": f"inputs larger than L2 ({N * (N + 1) * 8 / 1e9:.1f} GB matrix)",
                    "timed_region": "factor + back substitution per step (device events); generation excluded"},
         "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),

@@ -331,10 +331,10 @@ struct GridSolver {
     cudaStream_t st = nullptr;
     cublasHandle_t hb = nullptr;
     double* A = nullptr;
-    double* arena = nullptr;       // gathered panel + pack buffer (factor phase), then W + U12 buffers
+    double* arena = nullptr;       // factor phase: gathered panel, pack buffer, inner residues; update phase: W, U12, W residues
     size_t arena_elems = 0;
-    void* wres = nullptr;          // residues of W (A part)
-    void* win = nullptr;           // residues of inner-update L21 (A part)
+    void* wres = nullptr;          // residues of W (A part), inside the arena
+    void* win = nullptr;           // residues of inner-update L21 (A part), inside the arena
     double* linv = nullptr;        // inv(L11)
     void* wlinv = nullptr;         // its residues
     double* xch = nullptr;         // exchange buffers (3 x 2 NB x kXchCols)
@@ -380,7 +380,6 @@ struct GridSolver {
         const size_t bytesA = (size_t)lda * (size_t)nloc * 8;
         const size_t g_elems = (g->P > 1) ? (size_t)N * NB + (size_t)(mloc + NB) * NB : 0;  // gathered panel + pack
         const size_t wu_elems = (size_t)mloc * NB + (size_t)NB * nloc;                       // W + U12
-        arena_elems = std::max(g_elems, wu_elems);
         size_t tot = 0, wa = 0, wb = 0, tin = 0, ain = 0, bin = 0, tl = 0, al = 0, bl = 0;
         const int64_t mmax = std::max<int64_t>(std::max(mloc, (g->P > 1) ? N : mloc), NB);
         CHPL_TRY(chpl_oz2_worksize((size_t)mloc, (size_t)std::min<int64_t>(emu.chunk + 1024, std::max<int64_t>(nloc, 1)),
@@ -391,7 +390,12 @@ struct GridSolver {
         const size_t xch_bytes = (size_t)3 * 2 * NB * kXchCols * 8;
         size_t freeB = 0, totB = 0;
         CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
-        const size_t need = bytesA + arena_elems * 8 + wa + ain + (size_t)NB * NB * 8 + al + xch_bytes + work_bytes +
+        // one arena, two phases that never overlap: factor = [gathered panel | pack | inner-update residues],
+        // update = [W | U12 | residues of W]
+        const size_t g_bytes = round_up(g_elems * 8, 256), wu_bytes = round_up(wu_elems * 8, 256);
+        const size_t arena_bytes = std::max(g_bytes + ain, wu_bytes + wa);
+        arena_elems = arena_bytes / 8;
+        const size_t need = bytesA + arena_bytes + (size_t)NB * NB * 8 + al + xch_bytes + work_bytes +
                             panel_work_bytes(mmax, NBp) + (size_t)N * 8 * 2 + (size_t)mloc * 8 + ((size_t)768 << 20);
         if (cfg.verbose && g->rank == 0)
             std::printf("GRID MEM PLAN (rank 0): local %lld x %lld, matrix %.2f GiB, total %.2f GiB of %.2f GiB free\n",
@@ -401,9 +405,9 @@ struct GridSolver {
             return CHPL_ERR_WORKSPACE;
         }
         CHPL_CUDA(cudaMalloc((void**)&A, std::max<size_t>(bytesA, 8)));
-        CHPL_CUDA(cudaMalloc((void**)&arena, std::max<size_t>(arena_elems, 1) * 8));
-        CHPL_CUDA(cudaMalloc(&wres, wa));
-        CHPL_CUDA(cudaMalloc(&win, ain));
+        CHPL_CUDA(cudaMalloc((void**)&arena, std::max<size_t>(arena_bytes, 256)));
+        win = reinterpret_cast<uint8_t*>(arena) + g_bytes;
+        wres = reinterpret_cast<uint8_t*>(arena) + wu_bytes;
         CHPL_CUDA(cudaMalloc((void**)&linv, (size_t)NB * NB * 8));
         CHPL_CUDA(cudaMalloc(&wlinv, al));
         CHPL_CUDA(cudaMalloc((void**)&xch, xch_bytes));
@@ -423,7 +427,7 @@ struct GridSolver {
     void destroy()
     {
         emu.collect();
-        void* ps[] = {A, arena, wres, win, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf};
+        void* ps[] = {A, arena, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf};
         for (void* p : ps)
             if (p) cudaFree(p);
         if (hb) cublasDestroy(hb);

@@ -140,8 +140,8 @@ def measured_peaks() -> dict:
 
 def traffic_per_unit():
     """DRAM bytes per int8 multiply-add of the GEMM kernel from the committed
-    ncu summary (profiles/oz2_gemm_kernel_c2.json), or None."""
-    p = os.path.join(ROOT, "profiles", "oz2_gemm_kernel_c2.json")
+    ncu summary (profiles/oz2_gemm_kernel_m8192_n8192_k4096_L11.json), or None."""
+    p = os.path.join(ROOT, "profiles", "oz2_gemm_kernel_m8192_n8192_k4096_L11.json")
     try:
         d = json.load(open(p))
         return d["dram_bytes"] / d["int8_macs"]

@@ -19,6 +19,14 @@ pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
 
+@pytest.fixture(params=["pair", "single"])
+def form(request, monkeypatch):
+    """Both forms of the GEMM kernel: CTA pairs (256 x 256 tiles, the default
+    above 128 rows) and single CTAs (128 x 256 tiles)."""
+    monkeypatch.setenv("CHPL_OZ2_FORM", request.param)
+    return request.param
+
+
 def _split_rows_gpu(A, L, opA=0):
     m, k = (A.shape[1], A.shape[0]) if opA else A.shape
     ldv, ldk = round_up(m, 128), round_up(k, 128)
@@ -100,8 +108,8 @@ def _products_gpu(ra, rb, m, n, k, L):
 
 
 @pytest.mark.parametrize("L", [11, 12])
-@pytest.mark.parametrize("mnk", [(128, 256, 128), (300, 520, 384), (77, 33, 1000)])
-def test_products_bitexact(cuda, L, mnk):
+@pytest.mark.parametrize("mnk", [(128, 256, 128), (300, 520, 384), (77, 33, 1000), (1000, 700, 256)])
+def test_products_bitexact(cuda, form, L, mnk):
     m, n, k = mnk
     rng = np.random.default_rng(m * 7 + n + L)
     ldva, ldvb, ldk = round_up(m, 128), round_up(n, 256), round_up(k, 128)
@@ -118,10 +126,37 @@ def test_products_bitexact(cuda, L, mnk):
         assert np.array_equal(P[l], ref), f"modulus {l}"
 
 
-def test_products_extreme_magnitude(cuda):
+def test_products_persistent_tiles(cuda, form):
+    """More tiles than resident CTAs (each CTA or pair loops over tiles), and a
+    last 256-row tile whose second half lies past m."""
+    L, m, n, k = 2, 2600, 2304, 128
+    rng = np.random.default_rng(5)
+    ra = np.zeros((L, round_up(m, 128), k), dtype=np.int8)
+    rb = np.zeros((L, round_up(n, 256), k), dtype=np.int8)
+    ra[:, :m] = rng.integers(-128, 128, size=(L, m, k))
+    rb[:, :n] = rng.integers(-128, 128, size=(L, n, k))
+    P = _products_gpu(ra, rb, m, n, k, L)
+    for l in range(L):
+        ref = ra[l, :m].astype(np.int64) @ rb[l, :n].astype(np.int64).T
+        assert np.array_equal(P[l], ref), f"modulus {l}"
+
+
+def test_gemm_persistent_tiles_bitexact(cuda, form):
+    m, n, k, L = 2600, 1100, 256, 11
+    rng = np.random.default_rng(17)
+    A = rng.uniform(-0.5, 0.5, (m, k)) * np.exp2(rng.integers(-20, 21, size=m))[:, None]
+    B = rng.uniform(-0.5, 0.5, (k, n))
+    C = rng.uniform(-0.5, 0.5, (m, n))
+    got = _gemm_gpu(A, B, C, L)
+    ref = oracle.oz2_gemm(A, B, C, L, mode=1)
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("m", [128, 256])
+def test_products_extreme_magnitude(cuda, m):
     """All residues at -128: the largest int32 accumulation at k = 8192."""
-    L, m, n, k = 2, 128, 256, 8192
-    ra = np.full((L, 128, k), -128, dtype=np.int8)
+    L, n, k = 2, 256, 8192
+    ra = np.full((L, m, k), -128, dtype=np.int8)
     rb = np.full((L, 256, k), -128, dtype=np.int8)
     P = _products_gpu(ra, rb, m, n, k, L)
     assert np.all(P == 128 * 128 * k)
@@ -144,7 +179,7 @@ def _gemm_gpu(A, B, C, L, alpha=-1.0, beta=1.0, opA=0, opB=0, ldc_pad=0):
 @pytest.mark.parametrize("L", [11, 12])
 @pytest.mark.parametrize("ops", [(0, 0), (1, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("mnk", [(130, 257, 200), (512, 300, 1000), (33, 17, 5)])
-def test_gemm_bitexact_vs_oracle_mirror(cuda, L, ops, mnk):
+def test_gemm_bitexact_vs_oracle_mirror(cuda, form, L, ops, mnk):
     m, n, k = mnk
     opA, opB = ops
     rng = np.random.default_rng(m + n + k + 10 * opA + 20 * opB + L)

@@ -105,7 +105,8 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": f(rows[0][2]),
                 "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
-                "power_w_max": max((f(r[3]) or 0.0) for r in rows)}
+                "power_w_max": max((f(r[3]) or 0.0) for r in rows),
+                "power_w_median": statistics.median([f(r[3]) or 0.0 for r in load])}
 
 
 # ----------------------------------------------------------------------------- helpers

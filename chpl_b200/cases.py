@@ -16,7 +16,7 @@ import torch
 from . import hpl, oz2
 
 
-def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool) -> dict:
+def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool, sustain: float = 0.0) -> dict:
     g = torch.Generator(device="cuda")
     g.manual_seed(42)
     A = torch.rand(k, m, dtype=torch.float64, device="cuda", generator=g) - 0.5   # column-major m x k
@@ -33,9 +33,26 @@ def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool) -> dict:
         if best is None or ph[0] + ph[1] < best[0] + best[1]:
             best = ph
     t = best[0] + best[1]
-    return {"case": "gemm", "m": m, "n": n, "k": k, "moduli": L, "split_ms": best[0] * 1e3, "gemm_ms": best[1] * 1e3,
-            "fp64eq_tflops": 2.0 * m * n * k / t / 1e12,
-            "kernel_int8_tops": 2.0 * m * n * (-(-k // 128) * 128) * L / best[1] / 1e12}
+    out = {"case": "gemm", "m": m, "n": n, "k": k, "moduli": L, "split_ms": best[0] * 1e3, "gemm_ms": best[1] * 1e3,
+           "fp64eq_tflops": 2.0 * m * n * k / t / 1e12,
+           "kernel_int8_tops": 2.0 * m * n * (-(-k // 128) * 128) * L / best[1] / 1e12}
+    if sustain > 0:
+        # back-to-back updates for `sustain` seconds: the rate under the power cap
+        import sys, os
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        from bench import ClockSampler
+        n_it = max(1, int(sustain / max(t, 1e-4)))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            e0.record()
+            for _ in range(n_it):
+                oz2.gemm(oz2.OP_N, oz2.OP_N, m, n, k, -1.0, A, m, B, k, 1.0, C, m, L, True, work)
+            e1.record()
+            torch.cuda.synchronize()
+        ts = e0.elapsed_time(e1) * 1e-3
+        out["sustained"] = {"iters": n_it, "s": ts, "fp64eq_tflops": n_it * 2.0 * m * n * k / ts / 1e12,
+                            "clocks": clk.summary()}
+    return out
 
 
 def panel_case(m: int, n: int, reps: int) -> dict:
@@ -74,6 +91,7 @@ def main() -> None:
     g.add_argument("--moduli", type=int, default=11)
     g.add_argument("--reps", type=int, default=3)
     g.add_argument("--scaled", action="store_true")
+    g.add_argument("--sustain", type=float, default=0.0, help="also run back to back for this many seconds")
     pn = sub.add_parser("panel")
     pn.add_argument("--m", type=int, default=65536)
     pn.add_argument("--n", type=int, default=1024)
@@ -92,7 +110,7 @@ def main() -> None:
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.what == "gemm":
-        print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled)), flush=True)
+        print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled, a.sustain)), flush=True)
     elif a.what == "panel":
         print(json.dumps(panel_case(a.m, a.n, a.reps)), flush=True)
     else:

@@ -32,6 +32,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -264,18 +265,32 @@ __global__ void __launch_bounds__(256) split_strided_kernel(const double* __rest
 // ----------------------------------------------------------------------------
 // tcgen05 int8 GEMM with fused modular reduction + CRT epilogue
 // ----------------------------------------------------------------------------
-constexpr int BM = 128;                 // tile rows (TMEM lanes)
+constexpr int BM = 128;                 // rows per CTA (TMEM lanes)
 constexpr int BN = 256;                 // tile columns (TMEM columns per accumulator)
 constexpr int BK = 128;                 // K bytes per stage (one 128 B swizzle row)
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;        // 16 KB
-constexpr int B_BYTES = BN * BK;        // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;       // double-buffered accumulator
-constexpr int GEMM_SMEM = 1024 + STAGES * STAGE_BYTES + 256;
 constexpr int SCRATCH_TILE = BM * BN;   // bytes per modulus per CTA
+
+// Two forms of the kernel share one body:
+//   single: one CTA computes a 128 x 256 tile; it stages A 128 x 128 and
+//           B 256 x 128 per K block (48 KB, 4 stages);
+//   pair:   a cluster of two CTAs computes a 256 x 256 tile with
+//           tcgen05.mma.cta_group::2 issued by the even CTA; each CTA stages
+//           its own 128 rows of A and 128 of the 256 B rows (32 KB, 6 stages),
+//           so one int8 MAC needs 2/3 of the shared-memory fill of the single
+//           form; each CTA's TMEM holds the accumulator of its 128 rows.
+template <bool PAIR>
+struct Form {
+    static constexpr int TBM = PAIR ? 2 * BM : BM;      // tile rows
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // B rows staged by one CTA
+    static constexpr int B_BYTES = B_ROWS * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+};
 
 struct GemmParams {
     int m, n;
@@ -321,10 +336,21 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, uin
     return mbar_wait(bar, parity, &never, limit_ns);
 }
 
+__device__ __forceinline__ void spin_ns(uint64_t ns)
+{
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < ns) {
+    }
+}
+
+template <bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     oz2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ GemmParams p)
 {
+    using F = Form<PAIR>;
+    constexpr int STAGES = F::STAGES;
+    constexpr int STAGE_BYTES = F::STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -336,57 +362,88 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = warp_id(), lane = lane_id();
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;   // 0: the CTA that issues the MMAs
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int nunits = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], EPI_WARPS); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], EPI_WARPS * (PAIR ? 2 : 1)); }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
-    if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+    if (warp == 1) {
+        if (PAIR) { tmem_alloc_pair(tmem_slot, TMEM_COLS); tmem_relinquish_pair(); }
+        else { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+    }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync(); else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int total = p.mtiles * p.ntiles;
     const int L = p.M.L;
+    // barriers of the MMA-issuing CTA, as shared::cluster addresses
+    const uint32_t lead_full = PAIR ? map_to_rank(smem_u32(full), 0) : 0u;
+    const uint32_t lead_acc_empty = PAIR ? map_to_rank(smem_u32(acc_empty), 0) : 0u;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (both CTAs of a pair) ----------------
         if (elect_one()) {
             int stage = 0;
             uint32_t ph = 0;
             int issued[STAGES];
             for (int s = 0; s < STAGES; ++s) issued[s] = -1;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int tile = unit; tile < total && ok; tile += nunits) {
                 int mt, nt;
                 tile_coords(p, tile, mt, nt);
+                const int rowA = mt * F::TBM + (int)rank * BM;
+                const int rowB = nt * BN + (int)rank * F::B_ROWS;
                 for (int l = 0; l < L && ok; ++l)
                     for (int kb = 0; kb < p.kblocks; ++kb) {
                         if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
                         uint8_t* sa = smem + stage * STAGE_BYTES;
-                        tma_load_2d(sa, &tmA, &full[stage], kb * BK, l * p.rowsA + mt * BM);
-                        tma_load_2d(sa + A_BYTES, &tmB, &full[stage], kb * BK, l * p.rowsB + nt * BN);
+                        if (PAIR) {
+                            // the even CTA's full barrier counts both CTAs' bytes
+                            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                            const uint32_t fb = lead_full + stage * 8;
+                            tma_load_2d_pair(sa, &tmA, fb, kb * BK, l * p.rowsA + rowA);
+                            tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * BK, l * p.rowsB + rowB);
+                        } else {
+                            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                            tma_load_2d(sa, &tmA, &full[stage], kb * BK, l * p.rowsA + rowA);
+                            tma_load_2d(sa + A_BYTES, &tmB, &full[stage], kb * BK, l * p.rowsB + rowB);
+                        }
                         issued[stage] = (int)ph;
                         if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                     }
             }
-            if (!ok)  // let the copies already in flight land before the CTA exits
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued[s] >= 0) bounded_wait(&full[s], (uint32_t)issued[s], 20000000ull);
+            if (!ok) {  // let the copies already in flight land before the CTA exits
+                if (PAIR) spin_ns(1000000ull);
+                else
+                    for (int s = 0; s < STAGES; ++s)
+                        if (issued[s] >= 0) bounded_wait(&full[s], (uint32_t)issued[s], 20000000ull);
+            } else if (PAIR) {
+                // producer tail: every stage's last release (a commit from the
+                // even CTA's MMA thread) has landed in this CTA's barriers
+                for (int s = 0; s < STAGES; ++s) {
+                    if (issued[stage] >= 0 && !mbar_wait(&empty[stage], ph ^ 1u, abort_flag)) break;
+                    if (++stage == STAGES) { stage = 0; ph ^= 1u; }
+                }
+            }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (elect_one()) {
-            const uint32_t idesc = idesc_i8(BM, BN);
+        // ---------------- MMA issuer (the even CTA of a pair) ----------------
+        if (rank == 0 && elect_one()) {
+            const uint32_t idesc = idesc_i8(F::TBM, BN);
+            const uint32_t peer_empty = PAIR ? map_to_rank(smem_u32(empty), 1) : 0u;
+            const uint32_t peer_acc_full = PAIR ? map_to_rank(smem_u32(acc_full), 1) : 0u;
             int stage = 0;
             uint32_t ph = 0, acc = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int tile = unit; tile < total && ok; tile += nunits) {
                 for (int l = 0; l < L && ok; ++l) {
                     const uint32_t buf = acc & 1u, aph = (acc >> 1) & 1u;
                     if (!mbar_wait(&acc_empty[buf], aph ^ 1u, abort_flag)) { ok = false; break; }
@@ -397,25 +454,46 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tc_fence_after();
                         const uint32_t a0 = smem_u32(smem + stage * STAGE_BYTES), b0 = a0 + A_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < BK / 32; ++kk)
-                            mma_i8(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                                   (kb | kk) ? 1u : 0u);
-                        mma_commit(&empty[stage]);
+                        for (int kk = 0; kk < BK / 32; ++kk) {
+                            const uint64_t ad = umma_desc_sw128(a0 + kk * 32), bd = umma_desc_sw128(b0 + kk * 32);
+                            if (PAIR) mma_i8_pair(d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                            else mma_i8(d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                        }
+                        if (PAIR) {
+                            mma_commit_pair(smem_u32(&empty[stage]));
+                            mma_commit_pair(peer_empty + stage * 8);
+                        } else {
+                            mma_commit(&empty[stage]);
+                        }
                         if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                     }
                     if (!ok) break;
-                    mma_commit(&acc_full[buf]);
+                    if (PAIR) {
+                        mma_commit_pair(smem_u32(&acc_full[buf]));
+                        mma_commit_pair(peer_acc_full + buf * 8);
+                    } else {
+                        mma_commit(&acc_full[buf]);
+                    }
                     ++acc;
                 }
             }
             if (!ok) {  // wait for the MMAs already issued before TMEM is released
-                mma_commit(drain);
+                if (PAIR) mma_commit_pair(smem_u32(drain));
+                else mma_commit(drain);
                 bounded_wait(drain, 0, 20000000ull);
+            } else if (PAIR) {
+                // accumulator tail: both CTAs' epilogues have released both
+                // buffers (their arrivals on this CTA's barriers have landed)
+                for (int t = 0; t < 2; ++t) {
+                    const uint32_t buf = acc & 1u, aph = (acc >> 1) & 1u;
+                    if (!mbar_wait(&acc_empty[buf], aph ^ 1u, abort_flag)) break;
+                    ++acc;
+                }
             }
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue ----------------
+        // ---------------- epilogue (both CTAs of a pair) ----------------
         const int ew = warp - 2;
         const int quarter = warp & 3;        // TMEM lane quarter this warp may access
         const int half = ew >> 2;            // column half of the 256-wide tile
@@ -424,10 +502,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         int8_t* scr = p.scratch + (size_t)blockIdx.x * L * SCRATCH_TILE;
         uint32_t acc = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        for (int tile = unit; tile < total && ok; tile += nunits) {
             int mt, nt;
             tile_coords(p, tile, mt, nt);
-            const int gi = mt * BM + row;
+            const int gi = mt * F::TBM + (int)rank * BM + row;
             for (int l = 0; l < L; ++l) {
                 const uint32_t buf = acc & 1u, aph = (acc >> 1) & 1u;
                 if (!mbar_wait(&acc_full[buf], aph, abort_flag)) { ok = false; break; }
@@ -449,7 +527,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (c == 3) {  // every column of this warp is in registers: release the accumulator early
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        if (lane == 0) {
+                            if (PAIR) mbar_arrive_cluster(lead_acc_empty + buf * 8);
+                            else mbar_arrive(&acc_empty[buf]);
+                        }
                     }
                     if (p.mode == 1) {
                         const int gj0 = nt * BN + half * 128 + c * 32;
@@ -526,11 +607,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     }
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync(); else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
     }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_status, CHPL_ERR_TIMEOUT);
 }
@@ -652,6 +735,51 @@ int split(cudaStream_t st, bool contiguous, const double* x, size_t ld, size_t n
     return CHPL_OK;
 }
 
+// The single form is the default: sustained under the 1 kW power cap it keeps
+// the SM clock near 1.5 GHz where the pair form drops to ~1.1 GHz (m = n =
+// 32768, k = 4096, 11 moduli: 163-166 vs 137-140 FP64-equivalent TFLOPS), although
+// per clock the pair form is ~15 % faster (tensor pipe 62 % vs 54 % active).
+// CHPL_OZ2_FORM=pair (read at every launch) selects the pair form for
+// updates of more than 128 rows.
+static bool use_pair(size_t m)
+{
+    const char* e = std::getenv("CHPL_OZ2_FORM");
+    return e && std::strcmp(e, "pair") == 0 && m > (size_t)BM;
+}
+
+// clusters of two CTAs of the pair kernel that can be resident at once on this device
+static int max_pair_clusters()
+{
+    static int dev_cached = -1, n_cached = 0;
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return num_sms() / 2;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev == dev_cached) return n_cached;
+    int n = 0;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)num_sms());
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = Form<true>::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaFuncSetAttribute(oz2_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Form<true>::SMEM) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, oz2_gemm_kernel<true>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = num_sms() / 2;
+    }
+    dev_cached = dev;
+    n_cached = n;
+    return n;
+}
+
 int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsigned L, const int8_t* ra, size_t rowsA,
                 const int8_t* rb, size_t rowsB, const int32_t* shiftA, const int32_t* shiftB, double alpha,
                 double beta, double* C, size_t ldc, int32_t* P, size_t ldp, int8_t* scratch, int grid_max)
@@ -663,20 +791,23 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
         return CHPL_ERR_INVALID;
     }
     if ((size_t)L * std::max(rowsA, rowsB) > 0x7fffffffull) { set_error("residue planes too tall"); return CHPL_ERR_UNSUPPORTED; }
+    const bool pair = use_pair(m);
     CUtensorMap tmA, tmB;
     CHPL_TRY(make_tmap_i8(&tmA, ra, kPad, (uint64_t)L * rowsA, BM));
-    CHPL_TRY(make_tmap_i8(&tmB, rb, kPad, (uint64_t)L * rowsB, BN));
+    CHPL_TRY(make_tmap_i8(&tmB, rb, kPad, (uint64_t)L * rowsB, pair ? Form<true>::B_ROWS : BN));
     GemmParams p;
     std::memset(&p, 0, sizeof(p));
+    const int tbm = pair ? Form<true>::TBM : BM;
     p.m = (int)m;
     p.n = (int)n;
-    p.mtiles = (int)((m + BM - 1) / BM);
+    p.mtiles = (int)((m + tbm - 1) / tbm);
     p.ntiles = (int)((n + BN - 1) / BN);
     p.kblocks = (int)(kPad / BK);
     p.rowsA = (int)rowsA;
     p.rowsB = (int)rowsB;
     p.mode = mode;
-    p.group_m = 16;
+    p.group_m = pair ? 8 : 16;
+    if (const char* g = std::getenv("CHPL_OZ2_GROUP_M")) p.group_m = std::max(1, std::atoi(g));
     p.C = C;
     p.ldc = (long long)ldc;
     p.P = P;
@@ -688,10 +819,34 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     p.scratch = scratch;
     p.M = *M;
     const int tiles = p.mtiles * p.ntiles;
-    const int grid = std::min(tiles, grid_max);
-    CHPL_CUDA(cudaFuncSetAttribute(oz2_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
-    oz2_gemm_kernel<<<grid, THREADS, GEMM_SMEM, st>>>(tmA, tmB, p);
-    CHPL_CUDA(cudaGetLastError());
+    if (!pair) {
+        const int grid = std::min(tiles, grid_max);
+        CHPL_CUDA(cudaFuncSetAttribute(oz2_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Form<false>::SMEM));
+        oz2_gemm_kernel<false><<<grid, THREADS, Form<false>::SMEM, st>>>(tmA, tmB, p);
+        CHPL_CUDA(cudaGetLastError());
+        return CHPL_OK;
+    }
+    // pairs: as many clusters of two as can be resident at once (the grid is
+    // persistent), at most grid_max CTAs (the CRT scratch holds grid_max tiles)
+    CHPL_CUDA(cudaFuncSetAttribute(oz2_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Form<true>::SMEM));
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = Form<true>::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int clusters = std::min(tiles, std::min(max_pair_clusters(), grid_max / 2));
+    if (clusters < 1) { set_error("gemm_launch: no CTA pair fits"); return CHPL_ERR_UNSUPPORTED; }
+    cfg.gridDim = dim3((unsigned)(2 * clusters));
+    CHPL_CUDA(cudaLaunchKernelEx(&cfg, oz2_gemm_kernel<true>, tmA, tmB, p));
     return CHPL_OK;
 }
 

@@ -21,8 +21,8 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
 @pytest.fixture(params=["pair", "single"])
 def form(request, monkeypatch):
-    """Both forms of the GEMM kernel: CTA pairs (256 x 256 tiles, the default
-    above 128 rows) and single CTAs (128 x 256 tiles)."""
+    """Both forms of the GEMM kernel: single CTAs (128 x 256 tiles, the
+    default) and CTA pairs (256 x 256 tiles, above 128 rows)."""
     monkeypatch.setenv("CHPL_OZ2_FORM", request.param)
     return request.param
 

@@ -96,7 +96,8 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
         if os.path.exists(s) and (force or _newer(out, [s, LIB] + hdrs)):
             _run(["g++", "-O2", "-std=c++17", "-I", INCLUDE, s, "-o", out, "-L", HERE, "-lchpl",
                   "-Wl,-rpath,$ORIGIN/..", "-Wl,-rpath," + os.path.join(CUDA, "lib64"),
-                  "-L" + os.path.join(CUDA, "lib64"), "-lcudart", "-lpthread", "-ldl"], verbose)
+                  "-I", os.path.join(CUDA, "include"), "-L" + os.path.join(CUDA, "lib64"), "-lcublas", "-lcudart", "-lpthread",
+                  "-ldl", "-Wall"], verbose)
     return LIB
 
 

@@ -267,7 +267,7 @@ struct Emu {
     const oz2::Moduli* M = nullptr;
     void* work = nullptr;   // B part + scratch + split temporaries
     int64_t chunk = 32768;
-    int64_t launches = 0;
+    int64_t launches = 0, gemm_n = 0;
     double ops = 0.0, flops = 0.0, kernel_s = 0.0;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
 
@@ -304,6 +304,7 @@ struct Emu {
             cudaEventRecord(e1, st);
             ev.push_back({e0, e1});
             launches += 2;
+            ++gemm_n;
             ops += 2.0 * (double)m * (double)w * (double)y.kPad * L;
             flops += 2.0 * (double)m * (double)w * (double)k;
             c += w;
@@ -578,6 +579,9 @@ struct GridSolver {
                 CHPL_TRY(rows_scatter(Ab, Rb, std::max(nr, 1), d_rcv, nr, nc));
             }
         }
+        CHPL_TRY(watchdog_sync(g, st, "interchanges"));
+        phase[1] += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        t0 = std::chrono::steady_clock::now();
         // ---- 4. U12 on the diagonal process row, down the process columns ----
         if (ntr > 0) {
             if (pr == ps) {
@@ -588,6 +592,9 @@ struct GridSolver {
                                                 (size_t)ntr, cudaMemcpyDeviceToDevice, st));
             }
             if (P > 1) CHPL_NCCL(ncclBroadcast(U, U, (size_t)K * ntr, ncclDouble, ps, g->col, st));
+            CHPL_TRY(watchdog_sync(g, st, "U12"));
+            phase[2] += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            t0 = std::chrono::steady_clock::now();
             // ---- 5. trailing update ----
             if (mW > 0) {
                 const double* Bp = (P > 1) ? U : A + lrb + tc0 * lda;
@@ -725,8 +732,10 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     res->passed = hinfo == 0 && std::isfinite(res->resid) && res->resid < cfg->threshold;
     s.emu.collect();
     res->phase_s[0] = s.phase[0];
+    res->phase_s[1] = s.phase[1];
+    res->phase_s[2] = s.phase[2];
     res->phase_s[4] = s.phase[3];
-    res->gemm_launches = (int64_t)0;
+    res->gemm_launches = s.emu.gemm_n;
     res->gemm_kernel_s = s.emu.kernel_s;
     res->gemm_int8_ops = s.emu.ops;
     res->gemm_fp64eq_flops = s.emu.flops;

@@ -134,6 +134,7 @@ def bench(a, workloads, metric, flops, ClockSampler) -> None:
     ops = sum(r.gemm_int8_ops for r in res)
     nl = sum(r.gemm_launches for r in res)
     launches = sum(r.n_launches for r in res)
+    phases = {p: max_over_ranks(sum(r.phases[p] for r in res) / a.steps) for p in hpl.PHASES}
     g.close()
     if rank == 0:
         out = {
@@ -146,6 +147,7 @@ def bench(a, workloads, metric, flops, ClockSampler) -> None:
                        "l2": "inputs larger than L2",
                        "timed_region": "factor + back substitution (device events, max over ranks)"},
             "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
+            "phases_s_max_over_ranks": phases,
             "roofline": {"bound": "tensor", "achieved": ops / gk / 1e12 if gk else None, "peak": None,
                          "unit": "TOPS (int8)", "frac": None, "traffic": None,
                          "kernel": "oz2_gemm_kernel (rank 0)", "launches": nl},

@@ -35,6 +35,7 @@
 #include <cinttypes>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <thread>
@@ -229,6 +230,39 @@ static int watchdog_sync(GridComm* g, cudaStream_t st, const char* what)
 }
 
 
+static bool getenv_flag(const char* name)
+{
+    const char* v = std::getenv(name);
+    return v && *v && std::strcmp(v, "0") != 0;
+}
+
+// watchdog_sync for one event of a stream (the host may run ahead of it)
+static int watchdog_event(GridComm* g, cudaEvent_t ev, const char* what)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return CHPL_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(e, what, __FILE__, __LINE__);
+        ncclResult_t ae = ncclSuccess;
+        if (g->world) ncclCommGetAsyncError(g->world, &ae);
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (ae != ncclSuccess || el > g->timeout_s) {
+            if (!g->aborted) {
+                if (g->row) ncclCommAbort(g->row);
+                if (g->col) ncclCommAbort(g->col);
+                if (g->world) ncclCommAbort(g->world);
+                g->row = g->col = g->world = nullptr;
+                g->aborted = true;
+            }
+            set_error("%s: %s after %.1f s; communicators aborted", what,
+                      ae != ncclSuccess ? "NCCL asynchronous error" : "timeout", el);
+            return ae != ncclSuccess ? CHPL_ERR_NCCL : CHPL_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
 // ---------------------------------------------------------------------------- interchange planning
 // Net effect of the swaps (J+i <-> J+piv[i]), i = 0..K-1 in order, as row
 // moves "dst receives the old contents of src", split for process row pr of P:
@@ -267,6 +301,7 @@ struct Emu {
     const oz2::Moduli* M = nullptr;
     void* work = nullptr;   // B part + scratch + split temporaries
     int64_t chunk = 32768;
+    int grid_cap = 0;       // > 0: persistent GEMM grid limit (SMs left to concurrent communication)
     int64_t launches = 0, gemm_n = 0;
     double ops = 0.0, flops = 0.0, kernel_s = 0.0;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
@@ -280,7 +315,7 @@ struct Emu {
         for (int64_t c = 0; c < n;) {
             int64_t w = std::min(chunk, n - c);
             if (n - c - w > 0 && n - c - w < 1024) w = n - c;
-            const oz2::Layout y = oz2::layout((size_t)m, (size_t)w, (size_t)k, L, true, false);
+            const oz2::Layout y = oz2::layout((size_t)m, (size_t)w, (size_t)k, L, true, false, grid_cap);
             uint8_t* pa = static_cast<uint8_t*>(wa);
             uint8_t* pb = static_cast<uint8_t*>(work) + y.b_off;
             int32_t* shA = reinterpret_cast<int32_t*>(pa + y.a_shift);
@@ -312,6 +347,19 @@ struct Emu {
         return CHPL_OK;
     }
 
+    // residues of A (m x k) into wa, the layout run() reads with split_a = false
+    int split_only(cudaStream_t st, void* wa, int64_t m, int64_t k, const double* A, int64_t lda)
+    {
+        if (m <= 0 || k <= 0) return CHPL_OK;
+        const oz2::Layout y = oz2::layout((size_t)m, 256, (size_t)k, L, true, false, grid_cap);
+        uint8_t* pa = static_cast<uint8_t*>(wa);
+        CHPL_TRY(oz2::split(st, false, A, (size_t)lda, (size_t)m, (size_t)k, L, M->alpha,
+                            reinterpret_cast<int8_t*>(pa + y.a_res), y.mPad, y.kPad, reinterpret_cast<int32_t*>(pa + y.a_shift),
+                            static_cast<uint8_t*>(work) + y.tmp_off));
+        launches += 4;
+        return CHPL_OK;
+    }
+
     void collect()
     {
         for (auto& p : ev) {
@@ -337,6 +385,12 @@ struct GridSolver {
     void* wres = nullptr;          // residues of W (A part), inside the arena
     void* win = nullptr;           // residues of inner-update L21 (A part), inside the arena
     double* linv = nullptr;        // inv(L11)
+    double* linv2 = nullptr;       // second inv(L11) slot (lookahead)
+    int64_t* piv2 = nullptr;       // second pivot slot (lookahead)
+    void* plan2 = nullptr;         // interchange plan of the trailing columns (lookahead)
+    cudaStream_t sm = nullptr;     // communication stream (lookahead)
+    bool la = false;               // P = 1 depth-1 lookahead schedule
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> panel_ev;
     void* wlinv = nullptr;         // its residues
     double* xch = nullptr;         // exchange buffers (3 x 2 NB x kXchCols)
     int* dlist = nullptr;          // device copies of exchange row lists
@@ -394,7 +448,9 @@ struct GridSolver {
         // one arena, two phases that never overlap: factor = [gathered panel | pack | inner-update residues],
         // update = [W | U12 | residues of W]
         const size_t g_bytes = round_up(g_elems * 8, 256), wu_bytes = round_up(wu_elems * 8, 256);
-        const size_t arena_bytes = std::max(g_bytes + ain, wu_bytes + wa);
+        la = g->P == 1 && g->Q > 1 && !getenv_flag("CHPL_GRID_SERIAL");
+        // lookahead: the factor of block s+1 (inner residues) runs while W_s's residues are live
+        const size_t arena_bytes = la ? wu_bytes + wa + ain : std::max(g_bytes + ain, wu_bytes + wa);
         arena_elems = arena_bytes / 8;
         const size_t need = bytesA + arena_bytes + (size_t)NB * NB * 8 + al + xch_bytes + work_bytes +
                             panel_work_bytes(mmax, NBp) + (size_t)N * 8 * 2 + (size_t)mloc * 8 + ((size_t)768 << 20);
@@ -407,8 +463,15 @@ struct GridSolver {
         }
         CHPL_CUDA(cudaMalloc((void**)&A, std::max<size_t>(bytesA, 8)));
         CHPL_CUDA(cudaMalloc((void**)&arena, std::max<size_t>(arena_bytes, 256)));
-        win = reinterpret_cast<uint8_t*>(arena) + g_bytes;
+        win = reinterpret_cast<uint8_t*>(arena) + (la ? wu_bytes + wa : g_bytes);
         wres = reinterpret_cast<uint8_t*>(arena) + wu_bytes;
+        if (la) {
+            CHPL_CUDA(cudaStreamCreateWithPriority(&sm, cudaStreamNonBlocking, hi));
+            CHPL_CUDA(cudaMalloc((void**)&linv2, (size_t)NB * NB * 8));
+            CHPL_CUDA(cudaMalloc((void**)&piv2, (size_t)NB * sizeof(int64_t)));
+            CHPL_CUDA(cudaMalloc(&plan2, laswp_work_bytes(NB)));
+            if (cfg.reserve_sms > 0) emu.grid_cap = std::max(1, oz2::num_sms() - cfg.reserve_sms);
+        }
         CHPL_CUDA(cudaMalloc((void**)&linv, (size_t)NB * NB * 8));
         CHPL_CUDA(cudaMalloc(&wlinv, al));
         CHPL_CUDA(cudaMalloc((void**)&xch, xch_bytes));
@@ -428,16 +491,24 @@ struct GridSolver {
     void destroy()
     {
         emu.collect();
-        void* ps[] = {A, arena, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf};
+        void* ps[] = {A, arena, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf, linv2, piv2, plan2};
         for (void* p : ps)
             if (p) cudaFree(p);
+        for (auto& e : panel_ev) {
+            cudaEventDestroy(e.first);
+            cudaEventDestroy(e.second);
+        }
+        panel_ev.clear();
+        if (sm) cudaStreamDestroy(sm);
         if (hb) cublasDestroy(hb);
         if (st) cudaStreamDestroy(st);
     }
 
     // exact partial pivoting LU of an m x K panel (ld) in place, internal
     // panels of width NBp; piv[i] relative to the panel top
-    int factor_panel(double* Pm, int64_t ldp, int64_t m, int64_t K)
+    int factor_panel(double* Pm, int64_t ldp, int64_t m, int64_t K) { return factor_panel_p(Pm, ldp, m, K, piv); }
+
+    int factor_panel_p(double* Pm, int64_t ldp, int64_t m, int64_t K, int64_t* piv)
     {
         const double one = 1.0;
         for (int64_t jp = 0; jp < K; jp += NBp) {
@@ -607,6 +678,132 @@ struct GridSolver {
         return CHPL_OK;
     }
 
+    // ---------------------------------------------------------------- 1 x Q lookahead
+    // With one process row every rank holds all rows: interchanges and U12
+    // are local, and the only exchange per block is the broadcast of its
+    // pivots, inv(L11) and W = L21 from the owner of the block column along
+    // the row.  Two streams per rank: `st` computes, `sm` communicates.  The
+    // owner of block s+1 first brings that block up to date with block s
+    // (interchanges, U12, W*U12 on its columns only), factors it and hands it
+    // to `sm`; only then does it update the rest of its columns, while the
+    // other ranks, which have no panel to factor, update all of theirs.  So
+    // no rank waits for a panel another rank is factoring unless its own
+    // update of the step is shorter (depth-1 lookahead, src/chpl_p2.cu:1620-1741).
+    // Slots: pivots and inv(L11) alternate by block parity; W (FP64) has one
+    // buffer, released as soon as its residues are split; the panel's inner
+    // update residues have their own region.
+    int64_t Kof(int64_t s) const { return std::min(NB, N - s * NB); }
+
+    // owner of block column s: factor it (rows J.., local columns from lc),
+    // inv(L11) into its slot, W = L21 into the W buffer
+    int factor_owned(int64_t s, int64_t lc, int64_t* pv, double* lv)
+    {
+        const int64_t J = s * NB, K = Kof(s);
+        cudaEvent_t e0, e1;
+        CHPL_CUDA(cudaEventCreate(&e0));
+        CHPL_CUDA(cudaEventCreate(&e1));
+        panel_ev.push_back({e0, e1});
+        CHPL_CUDA(cudaEventRecord(e0, st));
+        CHPL_TRY(factor_panel_p(A + J + lc * lda, lda, N - J, K, pv));
+        CHPL_CUDA(cudaEventRecord(e1, st));
+        CHPL_TRY(identity(st, lv, K));
+        const double one = 1.0;
+        CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K, K, &one,
+                                     A + J + lc * lda, lda, lv, K));
+        const int64_t mW = N - J - K;
+        if (mW > 0)
+            CHPL_CUDA(cudaMemcpy2DAsync(arena, (size_t)mW * 8, A + J + K + lc * lda, (size_t)lda * 8, (size_t)mW * 8,
+                                        (size_t)K, cudaMemcpyDeviceToDevice, st));
+        n_launch += 2;
+        return CHPL_OK;
+    }
+
+    // local columns [c0, c0 + nc) through block s: interchanges, U12 = inv(L11) A12, A22 -= W U12
+    int update_cols(int64_t s, int64_t c0, int64_t nc, const double* lv)
+    {
+        if (nc <= 0) return CHPL_OK;
+        const int64_t J = s * NB, K = Kof(s), mW = N - J - K;
+        CHPL_TRY(laswp_apply(st, A + J, (size_t)lda, c0, nc, K, plan2));
+        ++n_launch;
+        CHPL_TRY(emu.run(st, wlinv, true, K, nc, K, lv, K, A + J + c0 * lda, lda, A + J + c0 * lda, lda, 1.0, 0.0));
+        if (mW > 0)
+            CHPL_TRY(emu.run(st, wres, false, mW, nc, K, arena, mW, A + J + c0 * lda, lda, A + J + K + c0 * lda, lda, -1.0,
+                             1.0));
+        return CHPL_OK;
+    }
+
+    int run_p1()
+    {
+        const int Q = g->Q, qc = g->qc;
+        int64_t* Pv[2] = {piv, piv2};
+        double* Lv[2] = {linv, linv2};
+        std::vector<cudaEvent_t> evs;
+        auto mk = [&](cudaEvent_t* e) -> int {
+            CHPL_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+            evs.push_back(*e);
+            return CHPL_OK;
+        };
+        auto cleanup = [&]() { for (auto e : evs) cudaEventDestroy(e); };
+        cudaEvent_t start, evF = nullptr, evWfree = nullptr, evLfree[2] = {nullptr, nullptr}, prev_end = nullptr;
+        int rc = mk(&start);
+        if (rc == CHPL_OK) rc = (cudaEventRecord(start, st) == cudaSuccess) ? CHPL_OK : CHPL_ERR_CUDA;
+        if (rc == CHPL_OK) rc = (cudaStreamWaitEvent(sm, start, 0) == cudaSuccess) ? CHPL_OK : CHPL_ERR_CUDA;
+        if (rc == CHPL_OK && qc == 0) {   // prologue: block 0 on its owner
+            rc = factor_owned(0, 0, Pv[0], Lv[0]);
+            if (rc == CHPL_OK) rc = mk(&evF);
+            if (rc == CHPL_OK) cudaEventRecord(evF, st);
+        }
+        for (int64_t s = 0; s < nblk && rc == CHPL_OK; ++s) {
+            const int64_t J = s * NB, K = Kof(s), mW = N - J - K;
+            const int qs = (int)(s % Q), slot = (int)(s & 1);
+            // ---- communication: pivots, inv(L11), W of block s from its owner ----
+            if (qc == qs) {
+                cudaStreamWaitEvent(sm, evF, 0);
+            } else {
+                if (evWfree) cudaStreamWaitEvent(sm, evWfree, 0);
+                if (evLfree[slot]) cudaStreamWaitEvent(sm, evLfree[slot], 0);
+            }
+            ncclGroupStart();
+            ncclBroadcast(Pv[slot], Pv[slot], (size_t)K, ncclInt64, qs, g->row, sm);
+            ncclBroadcast(Lv[slot], Lv[slot], (size_t)K * K, ncclDouble, qs, g->row, sm);
+            if (mW > 0) ncclBroadcast(arena, arena, (size_t)mW * K, ncclDouble, qs, g->row, sm);
+            if (ncclGroupEnd() != ncclSuccess) { set_error("NCCL broadcast of block %lld failed", (long long)s); rc = CHPL_ERR_NCCL; break; }
+            cudaEvent_t evW;
+            if ((rc = mk(&evW)) != CHPL_OK) break;
+            cudaEventRecord(evW, sm);
+            // ---- computation ----
+            cudaStreamWaitEvent(st, evW, 0);
+            if ((rc = emu.split_only(st, wres, mW, K, arena, mW)) != CHPL_OK) break;
+            if ((rc = mk(&evWfree)) != CHPL_OK) break;
+            cudaEventRecord(evWfree, st);
+            const int64_t tc0 = local_extent(J + K, NB, Q, qc), ntr = nloc - tc0;
+            if (ntr > 0 && (rc = laswp_plan(st, Pv[slot], 0, K, plan2)) != CHPL_OK) break;
+            const bool own_next = s + 1 < nblk && (int)((s + 1) % Q) == qc;
+            int64_t urgent = 0;
+            if (own_next) {   // block s+1 first: bring it up to date, factor it, hand it to sm
+                urgent = Kof(s + 1);
+                if ((rc = update_cols(s, tc0, urgent, Lv[slot])) != CHPL_OK) break;
+                if ((rc = factor_owned(s + 1, tc0, Pv[slot ^ 1], Lv[slot ^ 1])) != CHPL_OK) break;
+                if ((rc = mk(&evF)) != CHPL_OK) break;
+                cudaEventRecord(evF, st);
+            }
+            if ((rc = update_cols(s, tc0 + urgent, ntr - urgent, Lv[slot])) != CHPL_OK) break;
+            if ((rc = mk(&evLfree[slot])) != CHPL_OK) break;
+            cudaEventRecord(evLfree[slot], st);
+            // keep the host at most one block ahead of the device
+            if (prev_end && (rc = watchdog_event(g, prev_end, "lookahead step")) != CHPL_OK) break;
+            prev_end = evLfree[slot];
+        }
+        if (rc == CHPL_OK) rc = watchdog_sync(g, sm, "lookahead communication");
+        if (rc == CHPL_OK) rc = watchdog_sync(g, st, "lookahead update");
+        for (auto& e : panel_ev) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, e.first, e.second) == cudaSuccess) phase[0] += ms * 1e-3;
+        }
+        cleanup();
+        return rc;
+    }
+
     // distributed back substitution U x = b' (b' in global column N)
     int back_solve()
     {
@@ -708,7 +905,9 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     cudaEventCreate(&t0);
     cudaEventCreate(&t1);
     cudaEventRecord(t0, s.st);
-    for (int64_t b = 0; b < s.nblk && rc == CHPL_OK; ++b) rc = s.block_step(b);
+    if (s.la) rc = s.run_p1();
+    else
+        for (int64_t b = 0; b < s.nblk && rc == CHPL_OK; ++b) rc = s.block_step(b);
     if (rc == CHPL_OK) rc = s.back_solve();
     if (rc != CHPL_OK) return finish(rc);
     cudaEventRecord(t1, s.st);
@@ -740,8 +939,7 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     res->gemm_int8_ops = s.emu.ops;
     res->gemm_fp64eq_flops = s.emu.flops;
     res->n_launches = s.n_launch + s.emu.launches;
-    res->n_emulated = s.emu.launches / 2;
-    res->gemm_launches = s.emu.launches / 2;
+    res->n_emulated = s.emu.gemm_n;
     if (x_out) {
         cudaError_t e = cudaMemcpy(x_out, s.x, (size_t)s.N * 8, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) return finish(cuda_fail(e, "x readback", __FILE__, __LINE__));

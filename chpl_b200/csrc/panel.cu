@@ -2,17 +2,26 @@
 //
 // Replaces the cusolverDnXgetrf call of src/chpl_single.cu:668-679.
 // Recursive (left half, interchanges + U12 + Schur update, right half), down to
-// base blocks of kBaseW columns.  A base block is factored by one cooperative
-// kernel over all SMs: every CTA keeps a contiguous range of the block's rows
-// in shared memory; per column a warp-shuffle argmax gives each CTA's
-// candidate, one bounded grid barrier publishes the candidates, every CTA
-// picks the same pivot (largest |a|, smallest row on ties, as LAPACK's
-// idamax), and all CTAs apply the interchange, the scaling and the rank-1
-// update to their rows.  The pivot row and the old diagonal row travel through
-// double-buffered global slots written before the barrier, so no CTA ever
-// reads a row another CTA is rewriting.  The recursion's FP64 GEMM / TRSM
-// steps are plain cuBLAS calls; interchanges use the device-built net
-// permutation of hpl_kernels.cu.
+// base blocks of at most 32 columns.  A base block is factored by one
+// cooperative kernel over up to all SMs: every CTA keeps a contiguous range of
+// the block's rows in shared memory, and the pivot of every column is found
+// with one exchange between the CTAs:
+//   * each CTA's candidate (largest |a| among its rows, smallest row on ties,
+//     as LAPACK's idamax) is published as one record: value, row, the
+//     candidate's whole row, and (CTA 0) the current diagonal row; then a
+//     per-CTA flag is released;
+//   * every CTA polls the flags, loads all records in the same round trip and
+//     reduces them to the same pivot, so the pivot row and the row it
+//     displaces arrive with the decision;
+//   * after the interchange only column j+1 is updated before the next
+//     candidates are published (the candidate row's other columns are updated
+//     on the fly for its record); the update of columns j+2.. runs while the
+//     exchange is in flight.
+// Every element still receives exactly the operations of the unblocked
+// right-looking algorithm (x = fma(-l, u, x), l = a * (1 / pivot)), in the
+// same order.  Records and flags are double-buffered by column parity.
+// The recursion's FP64 GEMM / TRSM steps are plain cuBLAS calls; interchanges
+// use the device-built net permutation of hpl_kernels.cu.
 #include <cublas_v2.h>
 
 #include <algorithm>
@@ -24,18 +33,23 @@
 
 namespace chpl {
 
-constexpr int kBaseW = 32;          // widest base block (16 when the rows do not fit on chip at 32)
+constexpr int kBaseW = 32;          // widest base block (16 / 8 when the rows do not fit on chip)
 constexpr int kPanelThreads = 256;
+constexpr int kPanelWarps = kPanelThreads / 32;
 constexpr int kSmemBytes = 217600;  // shared memory of one base-kernel CTA (rows x width x 8 B)
+constexpr int kMaxPanelCTAs = 1024;
 
 struct PanelSync {
     int err;       // a wait ran out of time
     int pad[63];
 };
 
-struct Cand {
-    double val;
-    long long row;
+// one CTA's candidate for one column
+struct __align__(16) PanelRec {
+    double val;            // |candidate|, -1 when the CTA has no row at or below the column
+    long long row;         // its row (block-relative)
+    double cand[kBaseW];   // the candidate's row, updated through the previous pivot
+    double top[kBaseW];    // CTA 0: the diagonal row, updated through the previous pivot
 };
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p)
@@ -50,131 +64,159 @@ __device__ __forceinline__ void st_release(unsigned int* p, unsigned int v)
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until every CTA's flag reaches `stamp` (flags are monotonic within one
-// panel call).  Thread b polls CTA b's flag, so the whole exchange costs one
-// L2 round trip after the last writer, with no atomics.  Bounded: on timeout
-// it raises sync->err and returns false.
-__device__ bool wait_flags(PanelSync* sync, const unsigned int* flags, unsigned int G, unsigned int stamp)
-{
-    int good = 1;
-    if (threadIdx.x < G) {
-        const uint64_t t0 = globaltimer();
-        uint32_t it = 0;
-        while ((int)(ld_acquire(&flags[threadIdx.x]) - stamp) < 0) {
-            if ((++it & 255u) == 0 && (*(volatile int*)&sync->err || globaltimer() - t0 > 1000000000ull)) {  // 1 s
-                atomicExch(&sync->err, 1);
-                good = 0;
-                break;
-            }
-        }
-    }
-    return __syncthreads_and(good) != 0;
-}
-
 __device__ __forceinline__ bool better(double v, long long r, double bv, long long br)
 {
     return v > bv || (v == bv && r < br);
 }
 
-// Factor the m x w block at A (ld) in place.  ipiv[j] = base_row + pivot row
-// (0-based, relative to the block top + base_row).  info: 1-based column of
-// the first exact zero pivot (+ info_off), left unchanged otherwise.
+// Factor the m x w block at A (ld) in place, w <= W.  ipiv[j] = base_row +
+// pivot row (block-relative).  info: 1-based column of the first exact zero
+// pivot (+ info_off), left unchanged otherwise.
+template <int W>
 __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __restrict__ A, long long ld, long long m,
                                                                     int w, long long rows_per, int64_t* __restrict__ ipiv,
                                                                     long long base_row, int* __restrict__ info,
                                                                     int info_off, PanelSync* sync, unsigned int* flags,
-                                                                    unsigned int sbase, Cand* cand, double* candrow,
-                                                                    double* toprow)
+                                                                    unsigned int sbase, PanelRec* recs)
 {
-    extern __shared__ double S[];  // column-major [kBaseW][rows_per]: conflict-free row-parallel access
-    __shared__ double pv[kBaseW], tv[kBaseW];
-    __shared__ Cand wbest[kPanelThreads / 32];
+    extern __shared__ double S[];  // column-major [W][rows_per]: conflict-free row-parallel access
+    __shared__ double pv[W], tv[W];
+    __shared__ double stage[kPanelWarps][W], stage_top[W];
+    __shared__ double wv[kPanelWarps];
+    __shared__ long long wr[kPanelWarps];
+    __shared__ int wt[kPanelWarps];
     __shared__ long long pivrow;
     __shared__ double pivval;
-    const unsigned int G = gridDim.x;
+    const int G = (int)gridDim.x;
     const long long r0 = (long long)blockIdx.x * rows_per;
     const long long r1 = min(m, r0 + rows_per);
     const int nr = (int)max(0LL, r1 - r0);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const long long kNone = 0x7fffffffffffffffLL;
 
-    // load own rows
     for (int e = tid; e < nr * w; e += blockDim.x) {
         const int i = e % nr, c = e / nr;
         S[c * rows_per + i] = A[(r0 + i) + (long long)c * ld];
     }
     __syncthreads();
 
-    // candidate of column j among own rows >= jmin, published to slot (j & 1)
-    auto publish = [&](int j, long long jmin) {
-        double bv = -1.0;
-        long long br = 0x7fffffffffffffffLL;
-        for (int i = tid; i < nr; i += blockDim.x) {
-            const long long gr = r0 + i;
-            if (gr < jmin) continue;
-            const double v = fabs(S[j * rows_per + i]);
-            if (better(v, gr, bv, br)) { bv = v; br = gr; }
-        }
+    // Publish this CTA's candidate (bv, br: this thread's best) for column jc.
+    // With upd, columns > jc of the published rows get pivot jc-1's update
+    // (multiplier stored in column jc-1, pivot row in pv), which the rows in
+    // shared memory receive only afterwards.
+    auto publish = [&](int jc, double bv, long long br, bool upd) {
         for (int o = 16; o; o >>= 1) {
             const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const long long orr = __shfl_xor_sync(0xffffffffu, br, o);
             if (better(ov, orr, bv, br)) { bv = ov; br = orr; }
         }
-        if (lane == 0) wbest[wid] = Cand{bv, br};
-        __syncthreads();
-        if (tid == 0) {
-            Cand b = wbest[0];
-            for (int q = 1; q < (int)(blockDim.x / 32); ++q)
-                if (better(wbest[q].val, wbest[q].row, b.val, b.row)) b = wbest[q];
-            cand[(j & 1) * G + blockIdx.x] = b;
-            pivrow = b.row;
+        __syncwarp();  // the lane that owns the warp's best row has written it
+        if (bv >= 0.0 && lane < w) {
+            const int i = (int)(br - r0);
+            double x = S[lane * rows_per + i];
+            if (upd && lane > jc) x = fma(-S[(jc - 1) * rows_per + i], pv[lane], x);
+            stage[wid][lane] = x;
+        }
+        if (lane == 0) { wv[wid] = bv; wr[wid] = br; }
+        if (blockIdx.x == 0 && wid == 0 && lane < w) {  // row jc lives in CTA 0, thread jc (warp 0)
+            double x = S[lane * rows_per + jc];
+            if (upd && lane > jc) x = fma(-S[(jc - 1) * rows_per + jc], pv[lane], x);
+            stage_top[lane] = x;
         }
         __syncthreads();
-        const long long br2 = pivrow;
-        if (br2 >= r0 && br2 < r1 && tid < w)
-            candrow[((size_t)(j & 1) * G + blockIdx.x) * kBaseW + tid] = S[tid * rows_per + (br2 - r0)];
-        // the owner of row j publishes it: it moves to the pivot's old place
-        if (j < w && j >= r0 && j < r1 && tid < w) toprow[(j & 1) * kBaseW + tid] = S[tid * rows_per + (j - r0)];
-        __syncthreads();  // the barrier orders every thread's slot writes before thread 0's release
-        if (tid == 0) {
+        if (wid == 0) {
+            double v = lane < kPanelWarps ? wv[lane] : -1.0;
+            long long r = lane < kPanelWarps ? wr[lane] : kNone;
+            int q = lane;
+            for (int o = 16; o; o >>= 1) {  // full butterfly: every lane ends with the CTA's best
+                const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const long long orr = __shfl_xor_sync(0xffffffffu, r, o);
+                const int oq = __shfl_xor_sync(0xffffffffu, q, o);
+                if (better(ov, orr, v, r)) { v = ov; r = orr; q = oq; }
+            }
+            PanelRec* rec = recs + (size_t)(jc & 1) * G + blockIdx.x;
+            if (lane < w) {
+                if (v >= 0.0) rec->cand[lane] = stage[q][lane];
+                if (blockIdx.x == 0) rec->top[lane] = stage_top[lane];
+            }
+            if (lane == 0) { rec->val = v; rec->row = r; }
             __threadfence();
-            st_release(&flags[blockIdx.x], sbase + (unsigned int)j + 1u);
+            __syncwarp();
+            if (lane == 0) st_release(&flags[blockIdx.x], sbase + (unsigned int)jc + 1u);
         }
     };
 
-    publish(0, 0);
+    {   // candidates of column 0
+        double bv = -1.0;
+        long long br = kNone;
+        for (int i = tid; i < nr; i += blockDim.x) {
+            const double v = fabs(S[i]);
+            if (better(v, r0 + i, bv, br)) { bv = v; br = r0 + i; }
+        }
+        publish(0, bv, br, false);
+    }
+
     for (int j = 0; j < w; ++j) {
-        if (!wait_flags(sync, flags, G, sbase + (unsigned int)j + 1u)) return;
-        // every CTA reduces the same candidates to the same pivot; each lane
-        // loads its candidates together with their rows (one round trip)
-        if (wid == 0) {
-            double bv = -1.0;
-            long long br = 0x7fffffffffffffffLL;
-            int bb = -1;
-            for (int b = lane; b < (int)G; b += 32) {
-                const Cand c = cand[(j & 1) * G + b];
-                if (better(c.val, c.row, bv, br)) { bv = c.val; br = c.row; bb = b; }
+        // ---- exchange: every CTA's record for column j ----
+        double cr[W];
+        double v = -1.0;
+        long long r = kNone;
+        int good = 1;
+        const unsigned int want = sbase + (unsigned int)j + 1u;
+        // bounded acquire-poll of CTA b's flag for column j
+        auto poll = [&](int b) {
+            const uint64_t t0 = globaltimer();
+            uint32_t it = 0;
+            while ((int)(ld_acquire(&flags[b]) - want) < 0) {
+                if ((++it & 255u) == 0 && (*(volatile int*)&sync->err || globaltimer() - t0 > 1000000000ull)) {  // 1 s
+                    atomicExch(&sync->err, 1);
+                    return false;
+                }
             }
-            double myrow[kBaseW];
-            if (bb >= 0) {
-                const double* src = candrow + ((size_t)(j & 1) * G + bb) * kBaseW;
+            return true;
+        };
+        if (tid < G) {
+            good = poll(tid) ? 1 : 0;
+            if (good) {  // the whole record in one round trip
+                const PanelRec* rec = recs + (size_t)(j & 1) * G + tid;
+                const double2 vr = __ldcg(reinterpret_cast<const double2*>(rec));
+                v = vr.x;
+                r = __double_as_longlong(vr.y);
+                const double2* cp = reinterpret_cast<const double2*>(rec->cand);
 #pragma unroll
-                for (int c = 0; c < kBaseW; ++c) myrow[c] = c < w ? src[c] : 0.0;
+                for (int c = 0; c < W / 2; ++c) {
+                    const double2 x = 2 * c < w ? __ldcg(cp + c) : make_double2(0.0, 0.0);
+                    cr[2 * c] = x.x;
+                    cr[2 * c + 1] = x.y;
+                }
             }
-            double bv0 = bv;
-            long long br0 = br;
-            for (int o = 16; o; o >>= 1) {
-                const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const long long orr = __shfl_xor_sync(0xffffffffu, br, o);
-                if (better(ov, orr, bv, br)) { bv = ov; br = orr; }
-            }
-            // the lane holding the winner publishes its row
-            if (bv0 == bv && br0 == br && bb >= 0) {
+        }
+        if (tid < w && good) {  // the diagonal row, one element per thread, from CTA 0's record
+            if (tid == 0 || poll(0)) tv[tid] = __ldcg(&(recs + (size_t)(j & 1) * G)->top[tid]);
+            else good = 0;
+        }
+        int t = tid;
+        for (int o = 16; o; o >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const long long orr = __shfl_xor_sync(0xffffffffu, r, o);
+            const int ot = __shfl_xor_sync(0xffffffffu, t, o);
+            if (better(ov, orr, v, r)) { v = ov; r = orr; t = ot; }
+        }
+        if (lane == 0) { wv[wid] = v; wr[wid] = r; wt[wid] = t; }
+        if (!__syncthreads_and(good)) return;
+        {
+            double bv = wv[0];
+            long long br = wr[0];
+            int bt = wt[0];
+            for (int q = 1; q < kPanelWarps; ++q)
+                if (better(wv[q], wr[q], bv, br)) { bv = wv[q]; br = wr[q]; bt = wt[q]; }
+            if (tid == bt) {
 #pragma unroll
-                for (int c = 0; c < kBaseW; ++c) if (c < w) pv[c] = myrow[c];
+                for (int c = 0; c < W; ++c)
+                    if (c < w) pv[c] = cr[c];
                 pivrow = br;
                 pivval = bv;
             }
-            if (lane < w) tv[lane] = toprow[(j & 1) * kBaseW + lane];
         }
         __syncthreads();
         const long long p = pivrow;
@@ -184,6 +226,10 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
             if (pivval == 0.0 && *info == 0) *info = info_off + j + 1;
         }
         const double rp = (piv != 0.0) ? 1.0 / piv : 0.0;
+        const bool next = j + 1 < w;
+        // ---- interchange, scale column j, update column j+1 and find its candidates ----
+        double bv = -1.0;
+        long long br = kNone;
         for (int i = tid; i < nr; i += blockDim.x) {
             const long long gr = r0 + i;
             double* x = &S[i];  // element c at x[c * rows_per]
@@ -196,11 +242,24 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
             if (gr > j && piv != 0.0) {
                 const double l = x[j * rows_per] * rp;
                 x[j * rows_per] = l;
-                for (int c = j + 1; c < w; ++c) x[c * rows_per] = fma(-l, pv[c], x[c * rows_per]);
+                if (next) x[(j + 1) * rows_per] = fma(-l, pv[j + 1], x[(j + 1) * rows_per]);
+            }
+            if (next && gr > j) {
+                const double a = fabs(x[(j + 1) * rows_per]);
+                if (better(a, gr, bv, br)) { bv = a; br = gr; }
             }
         }
-        __syncthreads();
-        if (j + 1 < w) publish(j + 1, j + 1);
+        if (!next) break;
+        publish(j + 1, bv, br, piv != 0.0);
+        // ---- the rest of pivot j's update, while the exchange is in flight ----
+        if (piv != 0.0 && j + 2 < w) {
+            for (int i = tid; i < nr; i += blockDim.x) {
+                if (r0 + i <= j) continue;
+                double* x = &S[i];
+                const double l = x[j * rows_per];
+                for (int c = j + 2; c < w; ++c) x[c * rows_per] = fma(-l, pv[c], x[c * rows_per]);
+            }
+        }
     }
     __syncthreads();
     for (int e = tid; e < nr * w; e += blockDim.x) {
@@ -228,8 +287,10 @@ static int handles(cudaStream_t st, PanelHandles** out)
         if (cublasCreate(&g_ph.hb) != CUBLAS_STATUS_SUCCESS) { set_error("cublasCreate failed"); return CHPL_ERR_CUDA; }
         int nsm = 0, per = 0;
         CHPL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        CHPL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, panel_base_kernel, kPanelThreads, kSmemBytes));
+        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        CHPL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, panel_base_kernel<32>, kPanelThreads, kSmemBytes));
         if (per < 1) { set_error("panel kernel does not fit on an SM"); return CHPL_ERR_UNSUPPORTED; }
         g_ph.grid = nsm;  // one CTA per SM: co-resident by construction
         g_ph.dev = dev;
@@ -242,10 +303,9 @@ static int handles(cudaStream_t st, PanelHandles** out)
 size_t panel_work_bytes(int64_t m, int64_t n)
 {
     (void)m;
-    const size_t G = 1024;  // upper bound on the grid
-    return round_up(sizeof(PanelSync), 256) + round_up(G * sizeof(unsigned int), 256) + round_up(2 * G * sizeof(Cand), 256) +
-           round_up(2 * G * kBaseW * sizeof(double), 256) + round_up(2 * kBaseW * sizeof(double), 256) +
-           laswp_work_bytes(std::max<int64_t>(n, 1)) + 256;
+    const size_t G = kMaxPanelCTAs;  // upper bound on the grid
+    return round_up(sizeof(PanelSync), 256) + round_up(G * sizeof(unsigned int), 256) +
+           round_up(2 * G * sizeof(PanelRec), 256) + laswp_work_bytes(std::max<int64_t>(n, 1)) + 256;
 }
 
 namespace {
@@ -255,9 +315,7 @@ struct PanelCtx {
     PanelHandles* h;
     PanelSync* sync;
     unsigned int* flags;
-    Cand* cand;
-    double* candrow;
-    double* toprow;
+    PanelRec* recs;
     void* plan;
     unsigned int sbase;  // barrier arrivals so far in this call
     int* info;
@@ -277,10 +335,10 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
         return CHPL_ERR_UNSUPPORTED;
     }
     long long ldl = (long long)lda, ml = (long long)m, rp = (long long)rows_per, br = (long long)base_row;
-    void* args[] = {&A, &ldl, &ml, &w, &rp, &ipiv, &br, &c.info, &info_off, &c.sync, &c.flags, &c.sbase, &c.cand,
-                    &c.candrow, &c.toprow};
-    CHPL_CUDA(cudaLaunchCooperativeKernel((const void*)panel_base_kernel, dim3(G), dim3(kPanelThreads), args, smem,
-                                          c.st));
+    void* args[] = {&A, &ldl, &ml, &w, &rp, &ipiv, &br, &c.info, &info_off, &c.sync, &c.flags, &c.sbase, &c.recs};
+    const void* fn = w <= 8 ? (const void*)panel_base_kernel<8>
+                   : w <= 16 ? (const void*)panel_base_kernel<16> : (const void*)panel_base_kernel<32>;
+    CHPL_CUDA(cudaLaunchCooperativeKernel(fn, dim3(G), dim3(kPanelThreads), args, smem, c.st));
     c.sbase += (unsigned int)w;
     return CHPL_OK;
 }
@@ -335,17 +393,13 @@ int panel_getrf(cudaStream_t st, int64_t m, int64_t n, double* A, size_t lda, in
     c.sync = reinterpret_cast<PanelSync*>(w);
     w += round_up(sizeof(PanelSync), 256);
     c.flags = reinterpret_cast<unsigned int*>(w);
-    w += round_up(1024 * sizeof(unsigned int), 256);
-    c.cand = reinterpret_cast<Cand*>(w);
-    w += round_up(2 * 1024 * sizeof(Cand), 256);
-    c.candrow = reinterpret_cast<double*>(w);
-    w += round_up(2 * 1024 * kBaseW * sizeof(double), 256);
-    c.toprow = reinterpret_cast<double*>(w);
-    w += round_up(2 * kBaseW * sizeof(double), 256);
+    w += round_up(kMaxPanelCTAs * sizeof(unsigned int), 256);
+    c.recs = reinterpret_cast<PanelRec*>(w);
+    w += round_up(2 * kMaxPanelCTAs * sizeof(PanelRec), 256);
     c.plan = w;
     c.sbase = 0;
     c.info = info;
-    CHPL_CUDA(cudaMemsetAsync(c.sync, 0, round_up(sizeof(PanelSync), 256) + 1024 * sizeof(unsigned int), st));
+    CHPL_CUDA(cudaMemsetAsync(c.sync, 0, round_up(sizeof(PanelSync), 256) + kMaxPanelCTAs * sizeof(unsigned int), st));
     return rec(c, A, (int64_t)lda, m, n, ipiv, base_row, 0);
 }
 

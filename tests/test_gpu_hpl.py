@@ -69,7 +69,9 @@ def test_laswp_bitexact(cuda, case):
     assert np.array_equal(from_dev(dA, nrows, ncols), ref)
 
 
-@pytest.mark.parametrize("mn", [(1000, 128), (4096, 1024), (257, 64), (300, 300), (65536, 160), (2000, 37)])
+# base widths 32 (most), 16 (139264 rows: 82 CTAs) and 8 (300000 rows: 89 CTAs)
+@pytest.mark.parametrize("mn", [(1000, 128), (4096, 1024), (257, 64), (300, 300), (65536, 160), (2000, 37),
+                                (139264, 48), (300000, 24)])
 def test_panel_getrf(cuda, mn):
     m, n = mn
     L = _lib.load()

@@ -34,7 +34,7 @@ METRIC = "HPL FP64-equiv TFLOPS (2/3N³+2N²)/t at 1/2/4/8 B200; scaled residual
 # per-GPU-count workloads: (N, NB, P, Q)
 WORKLOADS = {
     1: (139264, 1024, 1, 1),
-    2: (196608, 2048, 1, 2),
+    2: (196608, 4096, 1, 2),
     4: (278528, 2048, 2, 2),
     8: (393216, 4096, 2, 4),
 }

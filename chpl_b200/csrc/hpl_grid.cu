@@ -387,7 +387,9 @@ struct GridSolver {
     double* linv = nullptr;        // inv(L11)
     double* linv2 = nullptr;       // second inv(L11) slot (lookahead)
     int64_t* piv2 = nullptr;       // second pivot slot (lookahead)
-    void* plan2 = nullptr;         // interchange plan of the trailing columns (lookahead)
+    void* plan2 = nullptr;         // interchange plans of the trailing columns (lookahead), kPlanSwaps swaps each
+    static constexpr int64_t kPlanSwaps = 2048;    // swaps one device plan holds
+    static constexpr int64_t kPlanChunks = 8;      // NB <= 16384
     cudaStream_t sm = nullptr;     // communication stream (lookahead)
     bool la = false;               // P = 1 depth-1 lookahead schedule
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> panel_ev;
@@ -469,8 +471,11 @@ struct GridSolver {
             CHPL_CUDA(cudaStreamCreateWithPriority(&sm, cudaStreamNonBlocking, hi));
             CHPL_CUDA(cudaMalloc((void**)&linv2, (size_t)NB * NB * 8));
             CHPL_CUDA(cudaMalloc((void**)&piv2, (size_t)NB * sizeof(int64_t)));
-            CHPL_CUDA(cudaMalloc(&plan2, laswp_work_bytes(NB)));
-            if (cfg.reserve_sms > 0) emu.grid_cap = std::max(1, oz2::num_sms() - cfg.reserve_sms);
+            CHPL_CUDA(cudaMalloc(&plan2, kPlanChunks * round_up(laswp_work_bytes(kPlanSwaps), 256)));
+            // SMs the persistent GEMM leaves to the communication stream's kernels
+            const char* rs = std::getenv("CHPL_GRID_RESERVE_SMS");
+            const int reserve = (rs && *rs) ? std::atoi(rs) : (cfg.reserve_sms >= 0 ? cfg.reserve_sms : 8);
+            if (reserve > 0) emu.grid_cap = std::max(1, oz2::num_sms() - reserve);
         }
         CHPL_CUDA(cudaMalloc((void**)&linv, (size_t)NB * NB * 8));
         CHPL_CUDA(cudaMalloc(&wlinv, al));
@@ -723,8 +728,11 @@ struct GridSolver {
     {
         if (nc <= 0) return CHPL_OK;
         const int64_t J = s * NB, K = Kof(s), mW = N - J - K;
-        CHPL_TRY(laswp_apply(st, A + J, (size_t)lda, c0, nc, K, plan2));
-        ++n_launch;
+        for (int64_t k0 = 0; k0 < K; k0 += kPlanSwaps) {   // the block's swaps in order, one plan per chunk
+            const void* pl = static_cast<uint8_t*>(plan2) + (k0 / kPlanSwaps) * round_up(laswp_work_bytes(kPlanSwaps), 256);
+            CHPL_TRY(laswp_apply(st, A + J, (size_t)lda, c0, nc, std::min(kPlanSwaps, K - k0), pl));
+            ++n_launch;
+        }
         CHPL_TRY(emu.run(st, wlinv, true, K, nc, K, lv, K, A + J + c0 * lda, lda, A + J + c0 * lda, lda, 1.0, 0.0));
         if (mW > 0)
             CHPL_TRY(emu.run(st, wres, false, mW, nc, K, arena, mW, A + J + c0 * lda, lda, A + J + K + c0 * lda, lda, -1.0,
@@ -777,7 +785,10 @@ struct GridSolver {
             if ((rc = mk(&evWfree)) != CHPL_OK) break;
             cudaEventRecord(evWfree, st);
             const int64_t tc0 = local_extent(J + K, NB, Q, qc), ntr = nloc - tc0;
-            if (ntr > 0 && (rc = laswp_plan(st, Pv[slot], 0, K, plan2)) != CHPL_OK) break;
+            for (int64_t k0 = 0; ntr > 0 && k0 < K && rc == CHPL_OK; k0 += kPlanSwaps)
+                rc = laswp_plan(st, Pv[slot], k0, std::min(K, k0 + kPlanSwaps),
+                                static_cast<uint8_t*>(plan2) + (k0 / kPlanSwaps) * round_up(laswp_work_bytes(kPlanSwaps), 256));
+            if (rc != CHPL_OK) break;
             const bool own_next = s + 1 < nblk && (int)((s + 1) % Q) == qc;
             int64_t urgent = 0;
             if (own_next) {   // block s+1 first: bring it up to date, factor it, hand it to sm
@@ -978,9 +989,15 @@ extern "C" int chpl_grid_create(int P, int Q, int rank, const unsigned char* id,
     CHPL_CUDA(cudaGetDevice(&g->dev));
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof(u));
-    ncclResult_t r = ncclCommInitRank(&g->world, P * Q, u, rank);
-    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->pr, g->qc, &g->row, nullptr);   // same process row
-    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->qc, g->pr, &g->col, nullptr);   // same process column
+    // NCCL kernels run beside the persistent GEMM (lookahead): cap their CTAs
+    // (CHPL_NCCL_MAX_CTAS, default 8) so they fit in the SMs the GEMM leaves free
+    ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+    const char* mc = std::getenv("CHPL_NCCL_MAX_CTAS");
+    conf.maxCTAs = (mc && *mc) ? std::max(1, std::atoi(mc)) : 8;
+    conf.minCTAs = std::min(conf.minCTAs > 0 ? conf.minCTAs : 1, conf.maxCTAs);
+    ncclResult_t r = ncclCommInitRankConfig(&g->world, P * Q, u, rank, &conf);
+    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->pr, g->qc, &g->row, &conf);   // same process row
+    if (r == ncclSuccess) r = ncclCommSplit(g->world, g->qc, g->pr, &g->col, &conf);   // same process column
     if (r != ncclSuccess) {
         set_error("NCCL communicator setup failed: %s", ncclGetErrorString(r));
         delete g;

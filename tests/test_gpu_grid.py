@@ -24,9 +24,10 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, P, Q, N, NB, out):
+def _worker(rank, world, port, P, Q, N, NB, out, env=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    os.environ.update(env or {})
     from chpl_b200 import grid
     dist = grid.init_from_env(timeout_s=300)
     g = grid.Grid(P, Q, timeout_s=120)
@@ -37,13 +38,13 @@ def _worker(rank, world, port, P, Q, N, NB, out):
     dist.destroy_process_group()
 
 
-def _run_spawned(P, Q, N, NB):
+def _run_spawned(P, Q, N, NB, env=None):
     import torch.multiprocessing as mp
     world = P * Q
     ctx = mp.get_context("spawn")
     with ctx.Manager() as m:
         out = m.dict()
-        mp.start_processes(_worker, args=(world, _free_port(), P, Q, N, NB, out), nprocs=world, join=True,
+        mp.start_processes(_worker, args=(world, _free_port(), P, Q, N, NB, out, env), nprocs=world, join=True,
                            start_method="spawn")
         return dict(out)
 
@@ -89,3 +90,16 @@ def test_grid_2x2(cuda):
         passed, resid, x = out[rank]
         assert passed, resid
         assert np.allclose(x, xs, rtol=1e-6, atol=1e-8)
+
+
+def test_grid_1x2_lookahead_equals_serial(cuda):
+    """The 1 x Q lookahead only reorders work (urgent block first, column
+    chunks), so its solution is bit-identical to the serial block steps."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    N, NB = 4608, 512
+    la = _run_spawned(1, 2, N, NB)
+    se = _run_spawned(1, 2, N, NB, env={"CHPL_GRID_SERIAL": "1"})
+    for rank in range(2):
+        assert la[rank][0] and se[rank][0]
+        assert np.array_equal(la[rank][2], se[rank][2])

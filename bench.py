@@ -35,7 +35,7 @@ METRIC = "HPL FP64-equiv TFLOPS (2/3N³+2N²)/t at 1/2/4/8 B200; scaled residual
 WORKLOADS = {
     1: (139264, 1024, 1, 1),
     2: (196608, 4096, 1, 2),
-    4: (278528, 2048, 2, 2),
+    4: (278528, 4096, 2, 2),
     8: (393216, 4096, 2, 4),
 }
 CPU_SAMPLE_N = 32768
@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--moduli", type=int, default=11)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lookahead", action="store_true", help="SM-reserving depth-1 lookahead (default: serial)")
+    ap.add_argument("--grid", default="", help="process grid PxQ for N > 1 GPUs (default: 1x2, 2x2, 2x4)")
     return ap.parse_args()
 
 

@@ -197,9 +197,20 @@ static inline int grid1(long long work)
 struct GridComm {
     int P = 1, Q = 1, rank = 0, pr = 0, qc = 0, dev = 0;
     ncclComm_t world = nullptr, row = nullptr, col = nullptr;
+    ncclComm_t col2 = nullptr;   // second process-column communicator: the bulk exchanges of the lookahead
     double timeout_s = 300.0;
     bool aborted = false;
 };
+
+// abort every communicator of the grid (a rank stopped answering)
+static void abort_comms(GridComm* g)
+{
+    if (g->aborted) return;
+    for (ncclComm_t* c : {&g->row, &g->col, &g->col2, &g->world})
+        if (*c) ncclCommAbort(*c);
+    g->row = g->col = g->col2 = g->world = nullptr;
+    g->aborted = true;
+}
 
 // Wait for `st` with a host-side limit; on expiry abort the communicators so
 // that every rank's pending collectives end with an error instead of hanging.
@@ -214,13 +225,7 @@ static int watchdog_sync(GridComm* g, cudaStream_t st, const char* what)
         if (g->world) ncclCommGetAsyncError(g->world, &ae);
         const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (ae != ncclSuccess || el > g->timeout_s) {
-            if (!g->aborted) {
-                if (g->row) ncclCommAbort(g->row);
-                if (g->col) ncclCommAbort(g->col);
-                if (g->world) ncclCommAbort(g->world);
-                g->row = g->col = g->world = nullptr;
-                g->aborted = true;
-            }
+            abort_comms(g);
             set_error("%s: %s after %.1f s; communicators aborted", what,
                       ae != ncclSuccess ? "NCCL asynchronous error" : "timeout", el);
             return ae != ncclSuccess ? CHPL_ERR_NCCL : CHPL_ERR_TIMEOUT;
@@ -248,13 +253,7 @@ static int watchdog_event(GridComm* g, cudaEvent_t ev, const char* what)
         if (g->world) ncclCommGetAsyncError(g->world, &ae);
         const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (ae != ncclSuccess || el > g->timeout_s) {
-            if (!g->aborted) {
-                if (g->row) ncclCommAbort(g->row);
-                if (g->col) ncclCommAbort(g->col);
-                if (g->world) ncclCommAbort(g->world);
-                g->row = g->col = g->world = nullptr;
-                g->aborted = true;
-            }
+            abort_comms(g);
             set_error("%s: %s after %.1f s; communicators aborted", what,
                       ae != ncclSuccess ? "NCCL asynchronous error" : "timeout", el);
             return ae != ncclSuccess ? CHPL_ERR_NCCL : CHPL_ERR_TIMEOUT;
@@ -392,10 +391,21 @@ struct GridSolver {
     static constexpr int64_t kPlanChunks = 8;      // NB <= 16384
     cudaStream_t sm = nullptr;     // communication stream (lookahead)
     bool la = false;               // P = 1 depth-1 lookahead schedule
+    bool la2 = false;              // P = 2 depth-1 lookahead schedule
+    cudaStream_t sb = nullptr;     // bulk communication stream (P = 2 lookahead)
+    double* Wd = nullptr;          // two W slots of mloc x NB; together the gathered panel (P = 2 lookahead)
+    double* pk = nullptr;          // pack buffer of the gather / scatter, kPackCols columns
+    double* Ub = nullptr;          // U12 of the bulk columns (K x nloc)
+    double* Uu = nullptr;          // two slots of U12 of the urgent block (K x NB each)
+    int64_t* hpiv = nullptr;       // pinned host copies of the two pivot slots
+    int* hlist = nullptr;          // pinned staging of the two exchange-list slots
+    cudaEvent_t evPk = nullptr;    // the chain partner's unpack has read the pack buffer
+    static constexpr int64_t kPackCols = 1024;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> panel_ev;
     void* wlinv = nullptr;         // its residues
     double* xch = nullptr;         // exchange buffers (3 x 2 NB x kXchCols)
     int* dlist = nullptr;          // device copies of exchange row lists
+    int* dlist2 = nullptr;         // second list slot (P = 2 lookahead)
     int64_t* piv = nullptr;        // pivots of the current block column (relative to J)
     int* info = nullptr;
     void* pwork = nullptr;
@@ -407,6 +417,9 @@ struct GridSolver {
     int64_t n_launch = 0;
     double phase[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     static constexpr int64_t kXchCols = 4096;
+
+    // the two W slots (mloc x NB each) and the gathered panel ((N - J) x NB at most) share Wd
+    size_t wd_elems() const { return (size_t)std::max<int64_t>(2 * mloc, N) * (size_t)NB; }
 
     int owner_row(int64_t gr) const { return (int)((gr / NB) % g->P); }
     int64_t local_row(int64_t gr) const { return (gr / NB / g->P) * NB + gr % NB; }
@@ -451,6 +464,33 @@ struct GridSolver {
         // update = [W | U12 | residues of W]
         const size_t g_bytes = round_up(g_elems * 8, 256), wu_bytes = round_up(wu_elems * 8, 256);
         la = g->P == 1 && g->Q > 1 && !getenv_flag("CHPL_GRID_SERIAL");
+        if (g->P == 2 && !getenv_flag("CHPL_GRID_SERIAL")) {
+            // P = 2 lookahead: W slots (also the gathered panel), W residues, inner-update residues,
+            // bulk and urgent U12, pack buffer; used instead of the arena
+            const size_t wd = round_up(wd_elems() * 8, 256);
+            const size_t need2 = bytesA + wd + wa + ain + round_up((size_t)NB * nloc * 8, 256) +
+                                 (size_t)2 * NB * NB * 8 + (size_t)(mloc + NB) * kPackCols * 8 + (size_t)2 * NB * NB * 8 +
+                                 al + xch_bytes + work_bytes + panel_work_bytes(mmax, NBp) + (size_t)N * 8 * 2 +
+                                 (size_t)mloc * 8 + ((size_t)1024 << 20);
+            // every rank must take the same schedule: the lookahead only if it fits on all of them
+            int fits = need2 <= freeB ? 1 : 0;
+            int* dfit = nullptr;
+            CHPL_CUDA(cudaMalloc((void**)&dfit, sizeof(int)));
+            CHPL_CUDA(cudaMemcpyAsync(dfit, &fits, sizeof(int), cudaMemcpyHostToDevice, st));
+            if (ncclAllReduce(dfit, dfit, 1, ncclInt, ncclMin, g->world, st) != ncclSuccess) {
+                cudaFree(dfit);
+                set_error("schedule agreement failed");
+                return CHPL_ERR_NCCL;
+            }
+            CHPL_CUDA(cudaMemcpyAsync(&fits, dfit, sizeof(int), cudaMemcpyDeviceToHost, st));
+            const int wrc = watchdog_sync(g, st, "schedule agreement");
+            cudaFree(dfit);
+            if (wrc != CHPL_OK) return wrc;
+            la2 = fits == 1;
+            if (cfg.verbose && g->rank == 0)
+                std::printf("GRID LOOKAHEAD PLAN (rank 0): %.2f GiB of %.2f GiB free -> %s\n", need2 / 1073741824.0,
+                            freeB / 1073741824.0, la2 ? "lookahead" : "serial steps");
+        }
         // lookahead: the factor of block s+1 (inner residues) runs while W_s's residues are live
         const size_t arena_bytes = la ? wu_bytes + wa + ain : std::max(g_bytes + ain, wu_bytes + wa);
         arena_elems = arena_bytes / 8;
@@ -459,14 +499,35 @@ struct GridSolver {
         if (cfg.verbose && g->rank == 0)
             std::printf("GRID MEM PLAN (rank 0): local %lld x %lld, matrix %.2f GiB, total %.2f GiB of %.2f GiB free\n",
                         (long long)mloc, (long long)nloc, bytesA / 1073741824.0, need / 1073741824.0, freeB / 1073741824.0);
-        if (need > freeB) {
+        if (!la2 && need > freeB) {
             set_error("grid memory plan: need %.2f GiB, %.2f GiB free (reduce N)", need / 1073741824.0, freeB / 1073741824.0);
             return CHPL_ERR_WORKSPACE;
         }
         CHPL_CUDA(cudaMalloc((void**)&A, std::max<size_t>(bytesA, 8)));
-        CHPL_CUDA(cudaMalloc((void**)&arena, std::max<size_t>(arena_bytes, 256)));
-        win = reinterpret_cast<uint8_t*>(arena) + (la ? wu_bytes + wa : g_bytes);
-        wres = reinterpret_cast<uint8_t*>(arena) + wu_bytes;
+        if (la2) {
+            CHPL_CUDA(cudaMalloc((void**)&Wd, wd_elems() * 8));
+            CHPL_CUDA(cudaMalloc(&wres, wa));
+            CHPL_CUDA(cudaMalloc(&win, ain));
+            CHPL_CUDA(cudaMalloc((void**)&Ub, std::max<size_t>((size_t)NB * nloc * 8, 256)));
+            CHPL_CUDA(cudaMalloc((void**)&Uu, (size_t)2 * NB * NB * 8));
+            CHPL_CUDA(cudaMalloc((void**)&pk, (size_t)(mloc + NB) * kPackCols * 8));
+            CHPL_CUDA(cudaMallocHost((void**)&hpiv, (size_t)2 * NB * sizeof(int64_t)));
+            CHPL_CUDA(cudaMallocHost((void**)&hlist, (size_t)2 * 8 * NB * sizeof(int)));
+            CHPL_CUDA(cudaEventCreateWithFlags(&evPk, cudaEventDisableTiming));
+            CHPL_CUDA(cudaStreamCreateWithPriority(&sm, cudaStreamNonBlocking, hi));
+            CHPL_CUDA(cudaStreamCreateWithPriority(&sb, cudaStreamNonBlocking, hi));
+            CHPL_CUDA(cudaMalloc((void**)&linv2, (size_t)NB * NB * 8));
+            CHPL_CUDA(cudaMalloc((void**)&piv2, (size_t)NB * sizeof(int64_t)));
+            CHPL_CUDA(cudaMalloc((void**)&dlist2, (size_t)4 * 2 * NB * sizeof(int)));
+            const char* rs = std::getenv("CHPL_GRID_RESERVE_SMS");
+            const int reserve = (rs && *rs) ? std::atoi(rs) : (cfg.reserve_sms >= 0 ? cfg.reserve_sms : 16);
+            if (reserve > 0) emu.grid_cap = std::max(1, oz2::num_sms() - reserve);
+        }
+        CHPL_CUDA(cudaMalloc((void**)&arena, la2 ? 256 : std::max<size_t>(arena_bytes, 256)));
+        if (!la2) {
+            win = reinterpret_cast<uint8_t*>(arena) + (la ? wu_bytes + wa : g_bytes);
+            wres = reinterpret_cast<uint8_t*>(arena) + wu_bytes;
+        }
         if (la) {
             CHPL_CUDA(cudaStreamCreateWithPriority(&sm, cudaStreamNonBlocking, hi));
             CHPL_CUDA(cudaMalloc((void**)&linv2, (size_t)NB * NB * 8));
@@ -493,12 +554,36 @@ struct GridSolver {
         return CHPL_OK;
     }
 
+    // streams drained within a few seconds (false: work is stuck behind an aborted peer)
+    bool streams_idle(double limit_s)
+    {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (cudaStream_t x : {st, sm, sb}) {
+            if (!x) continue;
+            while (cudaStreamQuery(x) == cudaErrorNotReady) {
+                if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit_s) return false;
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+            }
+        }
+        return true;
+    }
+
     void destroy()
     {
+        if (g && g->aborted && !streams_idle(10.0)) return;   // leave the memory to process exit rather than hang
         emu.collect();
-        void* ps[] = {A, arena, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf, linv2, piv2, plan2};
+        void* ps[] = {A, arena, linv, wlinv, xch, dlist, piv, info, pwork, plan, emu.work, x, tsum, vbuf, linv2, piv2, plan2,
+                      Wd, Ub, Uu, pk, dlist2};
         for (void* p : ps)
             if (p) cudaFree(p);
+        if (la2) {
+            if (wres) cudaFree(wres);
+            if (win) cudaFree(win);
+        }
+        if (hpiv) cudaFreeHost(hpiv);
+        if (hlist) cudaFreeHost(hlist);
+        if (evPk) cudaEventDestroy(evPk);
+        if (sb) cudaStreamDestroy(sb);
         for (auto& e : panel_ev) {
             cudaEventDestroy(e.first);
             cudaEventDestroy(e.second);
@@ -815,6 +900,285 @@ struct GridSolver {
         return rc;
     }
 
+    // ---------------------------------------------------------------- 2 x Q lookahead
+    // Streams per rank: `st` computes; `sm` carries the chain of the next
+    // block (pivot, inv(L11) and W broadcasts, the urgent interchanges and
+    // U12 of the process column that owns the next block, the gather and
+    // scatter of its panel) on the world / row / column communicators; `sb`
+    // carries the bulk interchanges and U12 broadcasts on a second column
+    // communicator, so a column pair's bulk exchange never queues behind the
+    // panel the other column pair is factoring.  In block step s the process
+    // column owning block s+1 updates that block first, gathers and factors
+    // it on its diagonal owner and hands pivots, inv(L11) and W to `sm`; all
+    // ranks then update the rest of their columns.  W alternates between two
+    // slots (one step of slack between the ranks of a process row); the
+    // gathered panel occupies both slots while it is factored, after the
+    // diagonal owner has split the current W into int8 residues.
+    struct Lists {
+        std::vector<int> lsrc, ldst, snd, rcv;
+    };
+
+    // interchanges of block s on local columns [c0, c0 + nc): local moves,
+    // rows across process rows on stream cs / communicator cm, in tiles
+    int exchange2(int64_t c0, int64_t nc, const int* dl, const Lists& Ls, cudaStream_t cs, ncclComm_t cm, cudaEvent_t e1,
+                  cudaEvent_t e2)
+    {
+        const int nl = (int)Ls.lsrc.size(), ns = (int)Ls.snd.size(), nr = (int)Ls.rcv.size();
+        if (nc <= 0 || (nl == 0 && ns == 0 && nr == 0)) return CHPL_OK;
+        const int *d_lsrc = dl, *d_ldst = dl + nl, *d_snd = dl + 2 * nl, *d_rcv = dl + 2 * nl + ns;
+        double* Tb = xch;
+        double* Sb2 = xch + (size_t)2 * NB * kXchCols;
+        double* Rb = xch + (size_t)4 * NB * kXchCols;
+        for (int64_t t0 = c0; t0 < c0 + nc; t0 += kXchCols) {
+            const int64_t n = std::min(kXchCols, c0 + nc - t0);
+            double* Ab = A + t0 * lda;
+            CHPL_TRY(rows_gather(Sb2, std::max(ns, 1), Ab, d_snd, ns, n));
+            CHPL_TRY(rows_gather(Tb, std::max(nl, 1), Ab, d_lsrc, nl, n));
+            if (ns > 0 || nr > 0) {
+                CHPL_CUDA(cudaEventRecord(e1, st));
+                CHPL_CUDA(cudaStreamWaitEvent(cs, e1, 0));
+                CHPL_NCCL(ncclGroupStart());
+                if (ns > 0) CHPL_NCCL(ncclSend(Sb2, (size_t)ns * n, ncclDouble, 1 - g->pr, cm, cs));
+                if (nr > 0) CHPL_NCCL(ncclRecv(Rb, (size_t)nr * n, ncclDouble, 1 - g->pr, cm, cs));
+                CHPL_NCCL(ncclGroupEnd());
+                CHPL_CUDA(cudaEventRecord(e2, cs));
+                CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));
+            }
+            CHPL_TRY(rows_scatter(Ab, Tb, std::max(nl, 1), d_ldst, nl, n));
+            CHPL_TRY(rows_scatter(Ab, Rb, std::max(nr, 1), d_rcv, nr, n));
+        }
+        return CHPL_OK;
+    }
+
+    // U12 of block s on local columns [c0, c0 + nc) (process row ps computes
+    // it in place and copies it to Ud, ld K), broadcast down the process
+    // column on cs / cm; every rank then reads U12 from Ud
+    int u12(int64_t s, int64_t c0, int64_t nc, const double* lv, double* Ud, cudaStream_t cs, ncclComm_t cm,
+            cudaEvent_t e1, cudaEvent_t e2)
+    {
+        if (nc <= 0) return CHPL_OK;
+        const int64_t J = s * NB, K = Kof(s);
+        const int ps = (int)(s % 2);
+        const int64_t lrb = local_extent(J, NB, 2, g->pr);
+        if (g->pr == ps) {
+            CHPL_TRY(emu.run(st, wlinv, true, K, nc, K, lv, K, A + lrb + c0 * lda, lda, A + lrb + c0 * lda, lda, 1.0, 0.0));
+            CHPL_CUDA(cudaMemcpy2DAsync(Ud, (size_t)K * 8, A + lrb + c0 * lda, (size_t)lda * 8, (size_t)K * 8, (size_t)nc,
+                                        cudaMemcpyDeviceToDevice, st));
+            CHPL_CUDA(cudaEventRecord(e1, st));
+            CHPL_CUDA(cudaStreamWaitEvent(cs, e1, 0));
+        }
+        CHPL_NCCL(ncclBroadcast(Ud, Ud, (size_t)K * nc, ncclDouble, ps, cm, cs));
+        CHPL_CUDA(cudaEventRecord(e2, cs));
+        CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));
+        return CHPL_OK;
+    }
+
+    // block s1 (global columns J1.., local columns from lc1) on its process
+    // column: the other process row sends its rows to the diagonal owner in
+    // chunks of kPackCols columns, the owner factors the gathered panel
+    // (exact partial pivoting) in the W slots and sends the rows back; then
+    // each rank of the column copies its W = L21 rows into W slot s1 & 1 and
+    // the owner computes inv(L11).  Returns with evF recorded where A1(s1)
+    // must wait (owner: st; partner: sm itself).
+    int chain_factor(int64_t s1, int64_t lc1, int64_t* pv, double* lv, cudaEvent_t evF, cudaEvent_t evG,
+                     cudaEvent_t e1, cudaEvent_t e2)
+    {
+        const int pr = g->pr, p1 = (int)(s1 % 2), partner = 1 - pr;
+        const int64_t J1 = s1 * NB, K1 = Kof(s1), mg = N - J1;
+        const int64_t lrb1 = local_extent(J1, NB, 2, pr), mact1 = mloc - lrb1;
+        const int64_t lrb1_o = local_extent(J1, NB, 2, partner), mact1_o = local_extent(N, NB, 2, partner) - lrb1_o;
+        const int64_t lrw1 = local_extent(J1 + K1, NB, 2, pr), mW1 = mloc - lrw1;
+        double* Wslot = Wd + (size_t)(s1 & 1) * mloc * NB;
+        if (pr == p1) {
+            CHPL_CUDA(cudaStreamWaitEvent(st, evPk, 0));   // an earlier unpack (as partner) has read pk
+            double* G = Wd;   // both W slots: (N - J1) x K1, ld mg
+            for (int64_t c0 = 0; c0 < K1; c0 += kPackCols) {
+                const int64_t nc = std::min(kPackCols, K1 - c0);
+                CHPL_CUDA(cudaEventRecord(e1, st));   // the previous chunk's shuffle has read pk
+                CHPL_CUDA(cudaStreamWaitEvent(sm, e1, 0));
+                CHPL_NCCL(ncclRecv(pk, (size_t)mact1_o * nc, ncclDouble, partner, g->col, sm));
+                CHPL_CUDA(cudaEventRecord(e2, sm));
+                CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));
+                panel_shuffle_kernel<<<grid1(mg * nc), 256, 0, st>>>(G + c0 * mg, mg, mg, nc, J1, NB, 2, pr,
+                                                                      A + lrb1 + (lc1 + c0) * lda, lda, lrb1, pk,
+                                                                      std::max<int64_t>(mact1_o, 1), lrb1_o, 0);
+                ++n_launch;
+            }
+            cudaEvent_t p0, p1e;
+            CHPL_CUDA(cudaEventCreate(&p0));
+            CHPL_CUDA(cudaEventCreate(&p1e));
+            panel_ev.push_back({p0, p1e});
+            CHPL_CUDA(cudaEventRecord(p0, st));
+            CHPL_TRY(factor_panel_p(G, mg, mg, K1, pv));
+            CHPL_CUDA(cudaEventRecord(p1e, st));
+            for (int64_t c0 = 0; c0 < K1; c0 += kPackCols) {
+                const int64_t nc = std::min(kPackCols, K1 - c0);
+                panel_shuffle_kernel<<<grid1(mg * nc), 256, 0, st>>>(G + c0 * mg, mg, mg, nc, J1, NB, 2, pr,
+                                                                      A + lrb1 + (lc1 + c0) * lda, lda, lrb1, pk,
+                                                                      std::max<int64_t>(mact1_o, 1), lrb1_o, 1);
+                ++n_launch;
+                CHPL_CUDA(cudaEventRecord(e1, st));
+                CHPL_CUDA(cudaStreamWaitEvent(sm, e1, 0));
+                CHPL_NCCL(ncclSend(pk, (size_t)mact1_o * nc, ncclDouble, partner, g->col, sm));
+                CHPL_CUDA(cudaEventRecord(e2, sm));
+                CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));   // pk is free again
+            }
+            CHPL_CUDA(cudaEventRecord(evG, st));   // the W slots hold no panel any more
+            CHPL_TRY(identity(st, lv, K1));
+            const double one = 1.0;
+            CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K1, K1,
+                                         &one, A + lrb1 + lc1 * lda, lda, lv, K1));
+            if (mW1 > 0)
+                CHPL_CUDA(cudaMemcpy2DAsync(Wslot, (size_t)mW1 * 8, A + lrw1 + lc1 * lda, (size_t)lda * 8, (size_t)mW1 * 8,
+                                            (size_t)K1, cudaMemcpyDeviceToDevice, st));
+            CHPL_CUDA(cudaEventRecord(evF, st));
+            n_launch += 2;
+        } else {
+            CHPL_CUDA(cudaStreamWaitEvent(st, evPk, 0));   // an earlier unpack has read pk
+            for (int64_t c0 = 0; c0 < K1; c0 += kPackCols) {
+                const int64_t nc = std::min(kPackCols, K1 - c0);
+                if (mact1 > 0)
+                    CHPL_CUDA(cudaMemcpy2DAsync(pk, (size_t)mact1 * 8, A + lrb1 + (lc1 + c0) * lda, (size_t)lda * 8,
+                                                (size_t)mact1 * 8, (size_t)nc, cudaMemcpyDeviceToDevice, st));
+                CHPL_CUDA(cudaEventRecord(e1, st));
+                CHPL_CUDA(cudaStreamWaitEvent(sm, e1, 0));
+                CHPL_NCCL(ncclSend(pk, (size_t)mact1 * nc, ncclDouble, p1, g->col, sm));
+                CHPL_CUDA(cudaEventRecord(e2, sm));
+                CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));   // pk is free again
+            }
+            // the factored rows come back on sm, which also unpacks them and copies W:
+            // this rank's computation goes on with its bulk update meanwhile
+            for (int64_t c0 = 0; c0 < K1; c0 += kPackCols) {
+                const int64_t nc = std::min(kPackCols, K1 - c0);
+                CHPL_NCCL(ncclRecv(pk, (size_t)mact1 * nc, ncclDouble, p1, g->col, sm));
+                if (mact1 > 0)
+                    CHPL_CUDA(cudaMemcpy2DAsync(A + lrb1 + (lc1 + c0) * lda, (size_t)lda * 8, pk, (size_t)mact1 * 8,
+                                                (size_t)mact1 * 8, (size_t)nc, cudaMemcpyDeviceToDevice, sm));
+            }
+            if (mW1 > 0)
+                CHPL_CUDA(cudaMemcpy2DAsync(Wslot, (size_t)mW1 * 8, A + lrw1 + lc1 * lda, (size_t)lda * 8, (size_t)mW1 * 8,
+                                            (size_t)K1, cudaMemcpyDeviceToDevice, sm));
+            CHPL_CUDA(cudaEventRecord(evF, sm));
+            CHPL_CUDA(cudaEventRecord(evG, sm));
+            CHPL_CUDA(cudaEventRecord(evPk, sm));   // st writes pk again only after this (next chain step)
+        }
+        return CHPL_OK;
+    }
+
+    int run_p2()
+    {
+        const int Q = g->Q, pr = g->pr, qc = g->qc;
+        int64_t* Pv[2] = {piv, piv2};
+        double* Lv[2] = {linv, linv2};
+        int* DL[2] = {dlist, dlist2};
+        std::vector<cudaEvent_t> evs;
+        auto mk = [&]() {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) evs.push_back(e);
+            return e;
+        };
+        cudaEvent_t start = mk(), evF = mk(), evG = mk(), e1 = mk(), e2 = mk(), e3 = mk(), e4 = mk(), evA = mk(),
+                    evPH = mk(), evWfree[2] = {mk(), mk()}, evLfree[2] = {mk(), mk()}, evEnd[2] = {mk(), mk()};
+        bool wfree_rec[2] = {false, false}, lfree_rec[2] = {false, false}, g_rec = false;
+        int rc = CHPL_OK;
+        auto done = [&](int r) {
+            for (auto e : evs) cudaEventDestroy(e);
+            return r;
+        };
+        for (auto e : evs)
+            if (!e) return done(cuda_fail(cudaErrorMemoryAllocation, "event", __FILE__, __LINE__));
+        CHPL_CUDA(cudaEventRecord(start, st));
+        CHPL_CUDA(cudaStreamWaitEvent(sm, start, 0));
+        CHPL_CUDA(cudaStreamWaitEvent(sb, start, 0));
+        // prologue: block 0 on process column 0
+        if (qc == 0) {
+            if ((rc = chain_factor(0, 0, Pv[0], Lv[0], evF, evG, e1, e2)) != CHPL_OK) return done(rc);
+            g_rec = true;
+        }
+        Lists Ls;
+        for (int64_t s = 0; s < nblk && rc == CHPL_OK; ++s) {
+            const int64_t J = s * NB, K = Kof(s);
+            const int ps = (int)(s % 2), qs = (int)(s % Q), slot = (int)(s & 1);
+            const int64_t lrw = local_extent(J + K, NB, 2, pr), mW = mloc - lrw;
+            const int64_t lrb = local_extent(J, NB, 2, pr);
+            double* Wslot = Wd + (size_t)slot * mloc * NB;
+            // ---- A1: pivots (world), inv(L11) and W (process rows) of block s ----
+            if (qc == qs && pr == ps) {
+                cudaStreamWaitEvent(sm, evF, 0);   // this rank factored block s
+            } else {
+                if (wfree_rec[slot]) cudaStreamWaitEvent(sm, evWfree[slot], 0);
+                if (lfree_rec[slot]) cudaStreamWaitEvent(sm, evLfree[slot], 0);
+                if (g_rec) cudaStreamWaitEvent(sm, evG, 0);
+            }
+            ncclGroupStart();
+            ncclBroadcast(Pv[slot], Pv[slot], (size_t)K, ncclInt64, 2 * qs + ps, g->world, sm);
+            if (ncclGroupEnd() != ncclSuccess) { rc = CHPL_ERR_NCCL; set_error("pivot broadcast failed"); break; }
+            ncclGroupStart();
+            if (pr == ps) ncclBroadcast(Lv[slot], Lv[slot], (size_t)K * K, ncclDouble, qs, g->row, sm);
+            if (mW > 0) ncclBroadcast(Wslot, Wslot, (size_t)mW * K, ncclDouble, qs, g->row, sm);
+            if (ncclGroupEnd() != ncclSuccess) { rc = CHPL_ERR_NCCL; set_error("W broadcast failed"); break; }
+            cudaEventRecord(evA, sm);
+            cudaMemcpyAsync(hpiv + (size_t)slot * NB, Pv[slot], (size_t)K * sizeof(int64_t), cudaMemcpyDeviceToHost, sm);
+            cudaEventRecord(evPH, sm);
+            // ---- computation ----
+            cudaStreamWaitEvent(st, evA, 0);
+            if ((rc = emu.split_only(st, wres, mW, K, Wslot, mW)) != CHPL_OK) break;
+            cudaEventRecord(evWfree[slot], st);
+            wfree_rec[slot] = true;
+            if ((rc = watchdog_event(g, evPH, "pivots")) != CHPL_OK) break;
+            plan_exchange(J, K, hpiv + (size_t)slot * NB, NB, 2, pr, Ls.lsrc, Ls.ldst, Ls.snd, Ls.rcv);
+            {   // lists to the device through this slot's pinned staging (its copy of two steps ago has run:
+                // the host waited for the end of step s-1)
+                int* hl = hlist + (size_t)slot * 8 * NB;
+                size_t n = 0;
+                for (const std::vector<int>* v : {&Ls.lsrc, &Ls.ldst, &Ls.snd, &Ls.rcv})
+                    for (int x : *v) hl[n++] = x;
+                if (n > (size_t)8 * NB) { rc = CHPL_ERR_INVALID; set_error("exchange lists overflow"); break; }
+                if (n) cudaMemcpyAsync(DL[slot], hl, n * sizeof(int), cudaMemcpyHostToDevice, st);
+            }
+            const int64_t tc0 = local_extent(J + K, NB, Q, qc), ntr = nloc - tc0;
+            const int q1 = (int)((s + 1) % Q);
+            const bool chain = s + 1 < nblk && qc == q1;
+            const int64_t urg = chain ? std::min<int64_t>(Kof(s + 1), ntr) : 0;
+            if (chain) {   // block s+1 first: interchanges, U12, update, then its factorization
+                if ((rc = exchange2(tc0, urg, DL[slot], Ls, sm, g->col, e1, e2)) != CHPL_OK) break;
+                double* Us = Uu + (size_t)slot * NB * NB;
+                if ((rc = u12(s, tc0, urg, Lv[slot], Us, sm, g->col, e1, e2)) != CHPL_OK) break;
+                if (mW > 0 &&
+                    (rc = emu.run(st, wres, false, mW, urg, K, Wslot, mW, Us, K, A + lrw + tc0 * lda, lda, -1.0, 1.0)) !=
+                        CHPL_OK)
+                    break;
+                if ((rc = chain_factor(s + 1, tc0, Pv[slot ^ 1], Lv[slot ^ 1], evF, evG, e1, e2)) != CHPL_OK) break;
+                g_rec = true;
+            }
+            // ---- the rest of the columns ----
+            const int64_t c0 = tc0 + urg, nc = ntr - urg;
+            if ((rc = exchange2(c0, nc, DL[slot], Ls, sb, g->col2, e3, e4)) != CHPL_OK) break;
+            if (nc > 0) {
+                if (s > 0) cudaStreamWaitEvent(sb, evEnd[slot ^ 1], 0);   // Ub is free (read by step s-1's update)
+                if ((rc = u12(s, c0, nc, Lv[slot], Ub, sb, g->col2, e3, e4)) != CHPL_OK) break;
+                if (mW > 0 &&
+                    (rc = emu.run(st, wres, false, mW, nc, K, Wslot, mW, Ub, K, A + lrw + c0 * lda, lda, -1.0, 1.0)) !=
+                        CHPL_OK)
+                    break;
+            }
+            (void)lrb;
+            cudaEventRecord(evLfree[slot], st);
+            lfree_rec[slot] = true;
+            cudaEventRecord(evEnd[slot], st);
+            // keep the host at most one block ahead of the device
+            if (s > 0 && (rc = watchdog_event(g, evEnd[slot ^ 1], "lookahead step")) != CHPL_OK) break;
+        }
+        if (rc == CHPL_OK) rc = watchdog_sync(g, sm, "lookahead chain");
+        if (rc == CHPL_OK) rc = watchdog_sync(g, sb, "lookahead bulk communication");
+        if (rc == CHPL_OK) rc = watchdog_sync(g, st, "lookahead update");
+        for (auto& e : panel_ev) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, e.first, e.second) == cudaSuccess) phase[0] += ms * 1e-3;
+        }
+        return done(rc);
+    }
+
     // distributed back substitution U x = b' (b' in global column N)
     int back_solve()
     {
@@ -917,6 +1281,7 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     cudaEventCreate(&t1);
     cudaEventRecord(t0, s.st);
     if (s.la) rc = s.run_p1();
+    else if (s.la2) rc = s.run_p2();
     else
         for (int64_t b = 0; b < s.nblk && rc == CHPL_OK; ++b) rc = s.block_step(b);
     if (rc == CHPL_OK) rc = s.back_solve();
@@ -998,6 +1363,7 @@ extern "C" int chpl_grid_create(int P, int Q, int rank, const unsigned char* id,
     ncclResult_t r = ncclCommInitRankConfig(&g->world, P * Q, u, rank, &conf);
     if (r == ncclSuccess) r = ncclCommSplit(g->world, g->pr, g->qc, &g->row, &conf);   // same process row
     if (r == ncclSuccess) r = ncclCommSplit(g->world, g->qc, g->pr, &g->col, &conf);   // same process column
+    if (r == ncclSuccess && P > 1) r = ncclCommSplit(g->world, g->qc, g->pr, &g->col2, &conf);
     if (r != ncclSuccess) {
         set_error("NCCL communicator setup failed: %s", ncclGetErrorString(r));
         delete g;
@@ -1019,6 +1385,7 @@ extern "C" int chpl_grid_destroy(void* grid)
     if (!g->aborted) {
         if (g->row) ncclCommDestroy(g->row);
         if (g->col) ncclCommDestroy(g->col);
+        if (g->col2) ncclCommDestroy(g->col2);
         if (g->world) ncclCommDestroy(g->world);
     }
     delete g;

@@ -106,6 +106,8 @@ def bench(a, workloads, metric, flops, ClockSampler) -> None:
     world = dist.get_world_size()
     rank = dist.get_rank()
     P, Q = grid_shape(world)
+    if getattr(a, "grid", ""):
+        P, Q = (int(v) for v in a.grid.lower().split("x"))
     N, NB = workloads.get(world, (a.N or 65536, a.NB or 2048))[:2]
     if a.N:
         N, NB = a.N, a.NB or NB

@@ -103,3 +103,21 @@ def test_grid_1x2_lookahead_equals_serial(cuda):
     for rank in range(2):
         assert la[rank][0] and se[rank][0]
         assert np.array_equal(la[rank][2], se[rank][2])
+
+
+@pytest.mark.parametrize("grid_shape,ngpu", [((2, 1), 2), ((2, 2), 4)])
+def test_grid_p2_lookahead_equals_serial(cuda, grid_shape, ngpu):
+    """The 2 x Q lookahead reorders work across three streams (urgent block,
+    chunked gather / scatter, bulk exchanges on a second communicator); the
+    solution is bit-identical to the serial block steps."""
+    if torch.cuda.device_count() < ngpu:
+        pytest.skip(f"needs {ngpu} GPUs")
+    P, Q = grid_shape
+    N, NB = 5000, 256
+    la = _run_spawned(P, Q, N, NB)
+    se = _run_spawned(P, Q, N, NB, env={"CHPL_GRID_SERIAL": "1"})
+    xs = _reference_x(N)
+    for rank in range(P * Q):
+        assert la[rank][0] and se[rank][0]
+        assert np.array_equal(la[rank][2], se[rank][2])
+        assert np.allclose(la[rank][2], xs, rtol=1e-6, atol=1e-8)

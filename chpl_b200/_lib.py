@@ -43,7 +43,7 @@ class HplConfig(ctypes.Structure):
 class HplResult(ctypes.Structure):
     _fields_ = [("time_s", _dbl), ("tflops", _dbl), ("resid", _dbl), ("passed", _int), ("matgen_s", _dbl),
                 ("phase_s", _dbl * 8), ("n_emulated", _i64), ("n_launches", _i64), ("gemm_launches", _i64),
-                ("gemm_kernel_s", _dbl), ("gemm_int8_ops", _dbl), ("gemm_fp64eq_flops", _dbl)]
+                ("gemm_kernel_s", _dbl), ("gemm_int8_ops", _dbl), ("gemm_fp64eq_flops", _dbl), ("schedule", _int)]
 
 
 # name -> (restype, argtypes); every function declared in include/chpl.h

@@ -400,7 +400,7 @@ struct GridSolver {
     int64_t* hpiv = nullptr;       // pinned host copies of the two pivot slots
     int* hlist = nullptr;          // pinned staging of the two exchange-list slots
     cudaEvent_t evPk = nullptr;    // the chain partner's unpack has read the pack buffer
-    static constexpr int64_t kPackCols = 1024;
+    static constexpr int64_t kPackCols = 512;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> panel_ev;
     void* wlinv = nullptr;         // its residues
     double* xch = nullptr;         // exchange buffers (3 x 2 NB x kXchCols)
@@ -431,7 +431,9 @@ struct GridSolver {
         cfg = c;
         N = c.N;
         NB = std::min<int64_t>(c.NB, N);
-        NBp = std::min<int64_t>(NB, c.agg > 0 ? std::max<int64_t>(1, NB / c.agg) : 1024);
+        // internal panel width of the block factorization: 1024, or 512 on two process rows (the
+        // gathered panel's inner-update residues then take half the memory)
+        NBp = std::min<int64_t>(NB, c.agg > 0 ? std::max<int64_t>(1, NB / c.agg) : (gc->P > 1 ? 512 : 1024));
         nblk = (N + NB - 1) / NB;
         mloc = local_extent(N, NB, g->P, g->pr);
         nloc = local_extent(N + 1, NB, g->Q, g->qc);
@@ -1306,6 +1308,7 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     if (rc != CHPL_OK) return finish(rc);
     res->passed = hinfo == 0 && std::isfinite(res->resid) && res->resid < cfg->threshold;
     s.emu.collect();
+    res->schedule = s.la || s.la2 ? 1 : 0;
     res->phase_s[0] = s.phase[0];
     res->phase_s[1] = s.phase[1];
     res->phase_s[2] = s.phase[2];
@@ -1354,6 +1357,10 @@ extern "C" int chpl_grid_create(int P, int Q, int rank, const unsigned char* id,
     CHPL_CUDA(cudaGetDevice(&g->dev));
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof(u));
+    // The grid's collectives are broadcasts, point-to-point pairs and tiny
+    // reductions: NVLink SHARP (NVLS) would only add multicast buffers to
+    // every communicator, so it is off unless the caller set it explicitly.
+    setenv("NCCL_NVLS_ENABLE", "0", 0);
     // NCCL kernels run beside the persistent GEMM (lookahead): cap their CTAs
     // (CHPL_NCCL_MAX_CTAS, default 8) so they fit in the SMs the GEMM leaves free
     ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;

@@ -72,7 +72,8 @@ class Grid:
                           passed=bool(r.passed), threshold=cfg.threshold, matgen_s=r.matgen_s,
                           phases={p: r.phase_s[i] for i, p in enumerate(hpl.PHASES)}, n_emulated=r.n_emulated,
                           n_launches=r.n_launches, gemm_launches=r.gemm_launches, gemm_kernel_s=r.gemm_kernel_s,
-                          gemm_int8_ops=r.gemm_int8_ops, gemm_fp64eq_flops=r.gemm_fp64eq_flops, x=x)
+                          gemm_int8_ops=r.gemm_int8_ops, gemm_fp64eq_flops=r.gemm_fp64eq_flops,
+                          schedule=r.schedule, x=x)
 
     def close(self) -> None:
         if self.handle:
@@ -146,6 +147,7 @@ def bench(a, workloads, metric, flops, ClockSampler) -> None:
             "data": "synthetic (chpl SplitMix64 generator, seed 42)",
             "config": {"workload": f"HPL solve N={N} NB={NB} {P}x{Q} grid, {a.moduli} moduli", "N": N, "NB": NB,
                        "grid": f"{P}x{Q}", "parallelism": f"2D block-cyclic P{P}Q{Q}",
+                       "schedule": "depth-1 lookahead" if all(r.schedule for r in res) else "serial block steps",
                        "l2": "inputs larger than L2",
                        "timed_region": "factor + back substitution (device events, max over ranks)"},
             "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),

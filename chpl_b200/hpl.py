@@ -147,6 +147,7 @@ class Result:
     gemm_kernel_s: float = 0.0
     gemm_int8_ops: float = 0.0
     gemm_fp64eq_flops: float = 0.0
+    schedule: int = 0
     x: np.ndarray | None = None
 
 

@@ -219,6 +219,7 @@ typedef struct chpl_hpl_result {
     double gemm_kernel_s;       /* their summed device time (CUDA events on their streams) */
     double gemm_int8_ops;       /* 2 * m * n * kPad * moduli summed over those launches */
     double gemm_fp64eq_flops;   /* 2 * m * n * k summed over those launches */
+    int schedule;               /* grid runs: 0 = serial block steps, 1 = depth-1 lookahead */
 } chpl_hpl_result;
 
 /* Fill cfg with the defaults of chpl_single / chpl_p2 (src/chpl_p2.cu:570-584). */

@@ -51,6 +51,7 @@ SIGNATURES = {
     "chpl_last_error_string": (ctypes.c_char_p, []),
     "chpl_version": (ctypes.c_char_p, []),
     "chpl_device_status": (_int, [ctypes.POINTER(_int)]),
+    "chpl_diag_bounded_wait": (_int, [_vp, _int, ctypes.c_uint64]),
     "chpl_oz2_worksize": (_int, [_sz, _sz, _sz, _uint, _int, _int, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                                  ctypes.POINTER(_sz)]),
     "chpl_oz2_gemm": (_int, [_vp, _int, _int, _sz, _sz, _sz, _dp, _vp, _sz, _vp, _sz, _dp, _vp, _sz, _uint, _int,

@@ -168,13 +168,6 @@ int main(int argc, char** argv)
     }
     const int P = size > 1 ? 2 : 1, Q = size / P;
     const Dat dat = read_dat(argc > 1 ? argv[1] : nullptr);
-    int ndev = 0;
-    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev < 1) {
-        std::fprintf(stderr, "[chpl_p2] rank %d: no CUDA device\n", rank);
-        return 1;
-    }
-    cudaSetDevice(local % ndev);
-
     chpl_hpl_config cfg;
     chpl_hpl_default_config(&cfg);
     cfg.N = dat.N;
@@ -202,13 +195,11 @@ int main(int argc, char** argv)
     const int port = env_int(kBPort, env_int(kMPort, 29500) + 17);
     const char* host = std::getenv("MASTER_ADDR") ? std::getenv("MASTER_ADDR") : "127.0.0.1";
 
-    chpl_hpl_result res;
-    const time_t ts0 = std::time(nullptr);
+    // the NCCL id first (host only): a rank that never shows up ends every
+    // other rank's bootstrap with an error after `timeout` seconds
+    unsigned char id[128] = {0};
     int rc = CHPL_OK;
-    if (size == 1) {
-        rc = chpl_hpl_run(&cfg, &res, nullptr);
-    } else {
-        unsigned char id[128] = {0};
+    if (size > 1) {
         if (rank == 0) {
             rc = chpl_grid_unique_id(id, sizeof(id));
             if (rc == CHPL_OK && !serve_id(port, size - 1, id, sizeof(id), timeout)) {
@@ -219,6 +210,19 @@ int main(int argc, char** argv)
             std::fprintf(stderr, "[chpl_p2] rank %d: no NCCL id from %s:%d within %.0f s\n", rank, host, port, timeout);
             return 1;
         }
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev < 1) {
+        std::fprintf(stderr, "[chpl_p2] rank %d: no CUDA device\n", rank);
+        return 1;
+    }
+    cudaSetDevice(local % ndev);
+
+    chpl_hpl_result res;
+    const time_t ts0 = std::time(nullptr);
+    if (size == 1) {
+        rc = chpl_hpl_run(&cfg, &res, nullptr);
+    } else {
         void* g = nullptr;
         if (rc == CHPL_OK) rc = chpl_grid_create(P, Q, rank, id, sizeof(id), 600.0, &g);
         if (rc == CHPL_OK) rc = chpl_grid_run(g, &cfg, &res, nullptr);

@@ -182,6 +182,16 @@ int chpl_panel_getrf_f64(void *stream, int64_t m, int64_t n, double *A, size_t l
  */
 int chpl_residual(void *stream, int64_t N, uint64_t seed, const double *x, double *resid);
 
+/*
+ * Failure-detection self-test (no reference counterpart): one bounded
+ * device-side wait on something nothing signals -- kind 0: an mbarrier phase
+ * (the wait every TMA / MMA / epilogue hand-off of the GEMM uses), kind 1: an
+ * acquire poll of a flag in global memory (the panel's cross-CTA exchange).
+ * Returns CHPL_ERR_TIMEOUT after limit_ns (<= 2 s) with the context still
+ * usable.  Synchronizes the stream.
+ */
+int chpl_diag_bounded_wait(void *stream, int kind, uint64_t limit_ns);
+
 /* ------------------------------------------------------------------------ */
 /* HPL solver                                                                */
 /* ------------------------------------------------------------------------ */

@@ -271,7 +271,7 @@ def main():
         run_single(a)
         return
     from chpl_b200 import grid
-    grid.bench(a, WORKLOADS, METRIC, flops, ClockSampler)
+    grid.bench(a, WORKLOADS, METRIC, flops, ClockSampler, int8_peak_tops, traffic_per_unit)
 
 
 if __name__ == "__main__":

@@ -1102,7 +1102,6 @@ struct GridSolver {
             const int64_t J = s * NB, K = Kof(s);
             const int ps = (int)(s % 2), qs = (int)(s % Q), slot = (int)(s & 1);
             const int64_t lrw = local_extent(J + K, NB, 2, pr), mW = mloc - lrw;
-            const int64_t lrb = local_extent(J, NB, 2, pr);
             double* Wslot = Wd + (size_t)slot * mloc * NB;
             // ---- A1: pivots (world), inv(L11) and W (process rows) of block s ----
             if (qc == qs && pr == ps) {
@@ -1164,7 +1163,6 @@ struct GridSolver {
                         CHPL_OK)
                     break;
             }
-            (void)lrb;
             cudaEventRecord(evLfree[slot], st);
             lfree_rec[slot] = true;
             cudaEventRecord(evEnd[slot], st);

@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lookahead", action="store_true", help="SM-reserving depth-1 lookahead (default: serial)")
     ap.add_argument("--grid", default="", help="process grid PxQ for N > 1 GPUs (default: 1x2, 2x2, 2x4)")
+    ap.add_argument("--e2e-leg", action="store_true",
+                    help="internal: the host-buffer end-to-end leg (run in a child process by the 1-GPU bench)")
     return ap.parse_args()
 
 
@@ -166,6 +168,123 @@ def cpu_baseline(N: int) -> dict:
             "resid": r}
 
 
+# ----------------------------------------------------------------------------- host-buffer end-to-end leg
+E2E_MARGIN = 16 << 30      # host bytes left free beside the pinned [A|b]
+E2E_MAX_STEPS = 2
+E2E_WARM_N = 8192
+
+
+def host_memory_available():
+    """Bytes the host can still give this job: MemAvailable, capped by the
+    cgroup's remaining limit when there is one (None if unknown)."""
+    avail = None
+    try:
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemAvailable:"):
+                    avail = int(ln.split()[1]) * 1024
+    except (OSError, ValueError):
+        pass
+    for lim_p, cur_p in (("/sys/fs/cgroup/memory.max", "/sys/fs/cgroup/memory.current"),
+                         ("/sys/fs/cgroup/memory/memory.limit_in_bytes", "/sys/fs/cgroup/memory/memory.usage_in_bytes")):
+        try:
+            with open(lim_p) as f:
+                lim = f.read().strip()
+            with open(cur_p) as f:
+                cur = int(f.read().strip())
+        except (OSError, ValueError):
+            continue
+        if lim != "max" and int(lim) < (1 << 60):
+            room = int(lim) - cur
+            avail = room if avail is None else min(avail, room)
+        break
+    return avail
+
+
+def e2e_order(N: int, NB: int):
+    """Order of the host-buffer leg: N when its pinned [A|b] fits in host memory
+    with a margin, else the largest multiple of NB that does; (None, why) when
+    not even N = 16384 fits."""
+    avail = host_memory_available()
+    if avail is None:
+        return None, "host memory size unknown"
+    budget = (avail - E2E_MARGIN) / 1.05
+    if N * (N + 1) * 8 <= budget:
+        return N, None
+    n = int((max(budget, 0.0) / 8.0) ** 0.5) // NB * NB
+    why = (f"[A|b] of N={N} needs {N * (N + 1) * 8 / 2**30:.0f} GiB of pinned host memory, "
+           f"{avail / 2**30:.0f} GiB available")
+    return (n, why) if n >= 16384 else (None, why)
+
+
+def run_e2e_leg(a) -> None:
+    """Child process: chpl_hpl_run_host (the public host-buffer call) per step,
+    wall clock; [A|b] in pinned host memory, copied in by the call (twice:
+    solve and verification) and x copied out."""
+    try:   # if the host runs short of memory, this process is the one to go
+        with open("/proc/self/oom_score_adj", "w") as f:
+            f.write("1000")
+    except OSError:
+        pass
+    from chpl_b200 import hpl
+    N, NB = a.N, a.NB
+    cfg = hpl.Config(N=N, NB=NB, moduli=a.moduli)
+    t0 = time.perf_counter()
+    S = hpl.HostSystem(N)
+    S.generate(cfg.seed)
+    setup = time.perf_counter() - t0
+    wn = min(N, E2E_WARM_N)
+    with hpl.HostSystem(wn) as W:       # warm-up at a small order: module load, allocator
+        W.generate(cfg.seed)
+        hpl.run_host(hpl.Config(N=wn, NB=min(NB, wn), moduli=a.moduli), W, verify=True)
+    walls, res = [], []
+    for _ in range(a.steps):
+        t = time.perf_counter()
+        r = hpl.run_host(cfg, S, verify=True)
+        walls.append(time.perf_counter() - t)
+        res.append(r)
+    S.close()
+    print(json.dumps({"value": a.steps * flops(N) / sum(walls) / 1e12, "steps": a.steps, "N": N, "NB": NB,
+                      "wall_s": walls, "device_s": [r.time_s for r in res], "h2d_s": [r.matgen_s for r in res],
+                      "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
+                      "setup_s": setup, "launches": sum(r.n_launches for r in res)}), flush=True)
+
+
+def e2e_host(a, N: int, NB: int, fallback: dict) -> dict:
+    """The e2e figure through chpl_hpl_run_host in a child process (so a host
+    that cannot hold the pinned system fails that process only).  Falls back to
+    `fallback` (the generated-input public call) with the reason."""
+    n, why = e2e_order(N, NB)
+    if n is None:
+        return dict(fallback, note=fallback["note"] + f"; host-buffer leg skipped: {why}")
+    steps = max(1, min(a.steps, E2E_MAX_STEPS))
+    cmd = [sys.executable, os.path.abspath(__file__), "--e2e-leg", "--N", str(n), "--NB", str(NB),
+           "--moduli", str(a.moduli), "--steps", str(steps)]
+    try:
+        p = subprocess.run(cmd, capture_output=True, text=True, timeout=1200)
+        leg = json.loads(p.stdout.strip().splitlines()[-1]) if p.returncode == 0 and p.stdout.strip() else None
+        err = None if leg else f"child exited {p.returncode}: {(p.stderr or p.stdout).strip()[-300:]}"
+    except (subprocess.TimeoutExpired, ValueError, IndexError) as ex:
+        leg, err = None, f"{type(ex).__name__}: {ex}"
+    if leg is None:
+        return dict(fallback, note=fallback["note"] + f"; host-buffer leg failed: {err}")
+    from chpl_b200 import _lib
+    nb = n * (n + 1) * 8
+    out = {"value": leg["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 2 * nb + ctypes.sizeof(_lib.HplConfig),
+           "d2h_bytes_per_step": n * 8 + ctypes.sizeof(_lib.HplResult), "steps": leg["steps"], "N": n, "NB": NB,
+           "resid": leg["resid"], "passed": leg["passed"],
+           "wall_s_per_step": sum(leg["wall_s"]) / len(leg["wall_s"]),
+           "device_solve_s_per_step": sum(leg["device_s"]) / len(leg["device_s"]),
+           "h2d_s_per_copy": sum(leg["h2d_s"]) / len(leg["h2d_s"]),
+           "gpu_launches": leg["launches"],
+           "note": "public host-buffer call chpl_hpl_run_host per step, wall clock: device allocation, [A|b] "
+                   "host->device from pinned memory, factor + solve, [A|b] host->device again and the HPL "
+                   "residual against it, x device->host; warm-up at N=%d" % min(n, E2E_WARM_N)}
+    if why:
+        out["note"] += f"; order reduced from N={N}: {why}"
+    return out
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(a) -> None:
     rank = int(os.environ.get("RANK", "0"))
@@ -249,14 +368,18 @@ def run_single(a) -> None:
         "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
         "phases_s": phases,
         "roofline": roof,
-        "e2e": {"value": a.steps * flops(N) / sum(walls) / 1e12, "unit": "TFLOPS",
-                "h2d_bytes_per_step": ctypes.sizeof(_lib.HplConfig),
-                "d2h_bytes_per_step": N * 8 + ctypes.sizeof(_lib.HplResult),
-                "note": "public API chpl_hpl_run per step (wall clock): allocation, on-device generation "
-                        "(HPL defines A,b as generated), solve, verification, x to host"},
+        "e2e": None,
         "gpu_launches": sum(r.n_launches for r in res),
         "clocks": clk.summary(),
     }
+    generated_e2e = {"value": a.steps * flops(N) / sum(walls) / 1e12, "unit": "TFLOPS",
+                     "h2d_bytes_per_step": ctypes.sizeof(_lib.HplConfig),
+                     "d2h_bytes_per_step": N * 8 + ctypes.sizeof(_lib.HplResult),
+                     "note": "public API chpl_hpl_run per step (wall clock): allocation, on-device generation "
+                             "of the HPL system, solve, verification, x to host"}
+    out["e2e_generated"] = generated_e2e
+    torch.cuda.empty_cache()
+    out["e2e"] = e2e_host(a, N, NB, generated_e2e)
     if not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(CPU_SAMPLE_N)
     print(json.dumps(out), flush=True)
@@ -266,6 +389,9 @@ def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+        return
+    if a.e2e_leg:
+        run_e2e_leg(a)
         return
     if a.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         run_single(a)

@@ -52,6 +52,8 @@ SIGNATURES = {
     "chpl_version": (ctypes.c_char_p, []),
     "chpl_device_status": (_int, [ctypes.POINTER(_int)]),
     "chpl_diag_bounded_wait": (_int, [_vp, _int, ctypes.c_uint64]),
+    "chpl_host_alloc": (_int, [_sz, ctypes.POINTER(_vp)]),
+    "chpl_host_free": (_int, [_vp]),
     "chpl_oz2_worksize": (_int, [_sz, _sz, _sz, _uint, _int, _int, ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                                  ctypes.POINTER(_sz)]),
     "chpl_oz2_gemm": (_int, [_vp, _int, _int, _sz, _sz, _sz, _dp, _vp, _sz, _vp, _sz, _dp, _vp, _sz, _uint, _int,
@@ -65,13 +67,16 @@ SIGNATURES = {
     "chpl_oz2_shift_bits": (_int, [_uint, _sz, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
     "chpl_matgen": (_int, [_vp, _vp, _sz, _sz, _sz, _i64, _i64, _i64, _u64]),
     "chpl_matgen_cyclic": (_int, [_vp, _vp, _sz, _i64, _i64, _int, _int, _int, _int, _u64]),
+    "chpl_matgen_host": (_int, [_i64, _u64, _vp, _sz]),
     "chpl_laswp_work_bytes": (_sz, [_i64, _i64]),
     "chpl_laswp": (_int, [_vp, _vp, _sz, _i64, _i64, _i64, _vp, _i64, _vp]),
     "chpl_panel_getrf_work_bytes": (_sz, [_i64, _i64]),
     "chpl_panel_getrf_f64": (_int, [_vp, _i64, _i64, _vp, _sz, _vp, _vp, _vp]),
     "chpl_residual": (_int, [_vp, _i64, _u64, _vp, _dp]),
+    "chpl_residual_matrix": (_int, [_vp, _i64, _vp, _sz, _vp, _dp]),
     "chpl_hpl_default_config": (None, [ctypes.POINTER(HplConfig)]),
     "chpl_hpl_run": (_int, [ctypes.POINTER(HplConfig), ctypes.POINTER(HplResult), _vp]),
+    "chpl_hpl_run_host": (_int, [ctypes.POINTER(HplConfig), _vp, _sz, _int, ctypes.POINTER(HplResult), _vp]),
     "chpl_grid_unique_id": (_int, [_vp, _sz]),
     "chpl_grid_create": (_int, [_int, _int, _int, _vp, _sz, _dbl, ctypes.POINTER(_vp)]),
     "chpl_grid_run": (_int, [_vp, ctypes.POINTER(HplConfig), ctypes.POINTER(HplResult), _vp]),

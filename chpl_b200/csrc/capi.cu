@@ -40,3 +40,17 @@ extern "C" int chpl_device_status(int* status)
     if (status) *status = a ? a : b;
     return CHPL_OK;
 }
+
+extern "C" int chpl_host_alloc(size_t bytes, void** ptr)
+{
+    if (!ptr || bytes == 0) { chpl::set_error("host_alloc: bad arguments"); return CHPL_ERR_INVALID; }
+    *ptr = nullptr;
+    CHPL_CUDA(cudaHostAlloc(ptr, bytes, cudaHostAllocPortable));
+    return CHPL_OK;
+}
+
+extern "C" int chpl_host_free(void* ptr)
+{
+    if (ptr) CHPL_CUDA(cudaFreeHost(ptr));
+    return CHPL_OK;
+}

@@ -27,6 +27,8 @@ int laswp_apply(cudaStream_t st, double* A, size_t lda, int64_t c0, int64_t ncol
 int ipiv_to_abs(cudaStream_t st, const int64_t* rel, int64_t n, int64_t base, int64_t* out);
 int identity(cudaStream_t st, double* X, int64_t n);
 int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid);
+// the same residual for [A | b] held in device memory (column N is b)
+int residual_matrix(cudaStream_t st, int64_t N, const double* Ab, size_t ld, const double* x, double* resid);
 int hpl_read_clear_status(int* st);
 size_t panel_work_bytes(int64_t m, int64_t n);
 // FP64 getrf of the m x n panel at A; ipiv[i] = base_row + pivot row within the panel

@@ -1,4 +1,5 @@
 // HPL building blocks on B200: matrix generation, row interchanges, residual.
+#include <algorithm>
 #include <cstdio>
 
 #include "common.cuh"
@@ -230,13 +231,33 @@ int identity(cudaStream_t st, double* X, int64_t n)
 }
 
 // ----------------------------------------------------------------------------
-// residual: regenerate A and b on the fly, deterministic two-stage reduction
+// residual: A and b regenerated on the fly (the generated system) or read from
+// a device copy of [A | b]; deterministic two-stage reduction
 // ----------------------------------------------------------------------------
 constexpr int kResChunks = 64;
 
-// part[(chunk*3 + 0)*N + i] = sum_j a_ij x_j, part[(chunk*3+1)*N + i] = sum |a_ij|
-// over the chunk's columns; one thread per row, columns walked in order.
-__global__ void __launch_bounds__(256) resid_partial_kernel(long long N, uint64_t seed, const double* __restrict__ x,
+// element (i, j) of the generated N x (N+1) system; column N is b
+struct GenSystem {
+    long long N;
+    uint64_t seed;
+    __device__ __forceinline__ double at(long long i, long long j) const
+    {
+        return hpl_elem(seed, (uint64_t)i * (uint64_t)(N + 1) + (uint64_t)j);
+    }
+};
+
+// element (i, j) of [A | b] held column-major in device memory
+struct DeviceSystem {
+    const double* Ab;
+    long long ld;
+    __device__ __forceinline__ double at(long long i, long long j) const { return Ab[i + j * ld]; }
+};
+
+// part[(chunk*2 + 0)*N + i] = sum_j a_ij x_j, part[(chunk*2+1)*N + i] = sum |a_ij|
+// over the chunk's columns; one thread per row, columns walked in order
+// (consecutive threads read consecutive rows of a column).
+template <class Sys>
+__global__ void __launch_bounds__(256) resid_partial_kernel(long long N, Sys sys, const double* __restrict__ x,
                                                             double* __restrict__ part)
 {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -245,9 +266,8 @@ __global__ void __launch_bounds__(256) resid_partial_kernel(long long N, uint64_
     const long long per = (N + kResChunks - 1) / kResChunks;
     const long long j0 = ch * per, j1 = min(N, j0 + per);
     double ax = 0.0, rs = 0.0;
-    const uint64_t base = (uint64_t)i * (uint64_t)(N + 1);
     for (long long j = j0; j < j1; ++j) {
-        const double a = hpl_elem(seed, base + (uint64_t)j);
+        const double a = sys.at(i, j);
         ax = fma(a, x[j], ax);
         rs += fabs(a);
     }
@@ -257,7 +277,8 @@ __global__ void __launch_bounds__(256) resid_partial_kernel(long long N, uint64_
 
 // per row: r_i = |sum_chunks ax - b_i|, rs_i = sum_chunks |a|; block maxima of
 // r, rs, |x|, |b| into out[blockIdx*4 + {0..3}]
-__global__ void __launch_bounds__(256) resid_rows_kernel(long long N, uint64_t seed, const double* __restrict__ x,
+template <class Sys>
+__global__ void __launch_bounds__(256) resid_rows_kernel(long long N, Sys sys, const double* __restrict__ x,
                                                          const double* __restrict__ part, double* __restrict__ out)
 {
     __shared__ double sm[4][256];
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(256) resid_rows_kernel(long long N, uint64_t s
             ax += part[(c * 2 + 0) * N + i];
             s += part[(c * 2 + 1) * N + i];
         }
-        const double b = hpl_elem(seed, (uint64_t)i * (uint64_t)(N + 1) + (uint64_t)N);
+        const double b = sys.at(i, N);
         r = fabs(ax - b);
         rs = s;
         xa = fabs(x[i]);
@@ -285,7 +306,8 @@ __global__ void __launch_bounds__(256) resid_rows_kernel(long long N, uint64_t s
     if (threadIdx.x < 4) out[blockIdx.x * 4 + threadIdx.x] = sm[threadIdx.x][0];
 }
 
-int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid)
+template <class Sys>
+static int residual_of(cudaStream_t st, int64_t N, Sys sys, const double* x, double* resid)
 {
     if (N <= 0) { set_error("residual: N <= 0"); return CHPL_ERR_INVALID; }
     const long long nb = (N + 255) / 256;
@@ -294,8 +316,8 @@ int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double*
     CHPL_CUDA(cudaMallocAsync((void**)&part, (size_t)kResChunks * 2 * N * sizeof(double), st));
     CHPL_CUDA(cudaMallocAsync((void**)&out, (size_t)nb * 4 * sizeof(double), st));
     dim3 g((unsigned)nb, kResChunks);
-    resid_partial_kernel<<<g, 256, 0, st>>>((long long)N, seed, x, part);
-    resid_rows_kernel<<<(unsigned)nb, 256, 0, st>>>((long long)N, seed, x, part, out);
+    resid_partial_kernel<Sys><<<g, 256, 0, st>>>((long long)N, sys, x, part);
+    resid_rows_kernel<Sys><<<(unsigned)nb, 256, 0, st>>>((long long)N, sys, x, part, out);
     CHPL_CUDA(cudaGetLastError());
     double* h = (double*)malloc((size_t)nb * 4 * sizeof(double));
     if (!h) { set_error("out of host memory"); return CHPL_ERR_WORKSPACE; }
@@ -317,6 +339,17 @@ int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double*
     return CHPL_OK;
 }
 
+int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid)
+{
+    return residual_of(st, N, GenSystem{(long long)N, seed}, x, resid);
+}
+
+int residual_matrix(cudaStream_t st, int64_t N, const double* Ab, size_t ld, const double* x, double* resid)
+{
+    if (!Ab || !x || (int64_t)ld < N) { set_error("residual: bad matrix arguments"); return CHPL_ERR_INVALID; }
+    return residual_of(st, N, DeviceSystem{Ab, (long long)ld}, x, resid);
+}
+
 int hpl_read_clear_status(int* st)
 {
     int v = 0, z = 0;
@@ -335,6 +368,31 @@ extern "C" int chpl_matgen(void* stream, double* A, size_t lda, size_t m, size_t
 {
     if (lda < m) { set_error("lda < m"); return CHPL_ERR_INVALID; }
     return matgen((cudaStream_t)stream, A, lda, m, n, row0, col0, ncg, seed);
+}
+
+extern "C" int chpl_matgen_host(int64_t N, uint64_t seed, double* Ab, size_t ldab)
+{
+    if (N <= 0 || !Ab || (int64_t)ldab < N) { set_error("matgen_host: bad arguments"); return CHPL_ERR_INVALID; }
+    // column blocks of <= 256 MiB generated on the device and copied out
+    const int64_t ncols = N + 1;
+    const int64_t per = std::max<int64_t>(1, std::min<int64_t>(ncols, ((int64_t)256 << 20) / (N * 8)));
+    double* d = nullptr;
+    cudaStream_t st = nullptr;
+    CHPL_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    cudaError_t e = cudaMalloc((void**)&d, (size_t)N * (size_t)per * sizeof(double));
+    int rc = e == cudaSuccess ? CHPL_OK : cuda_fail(e, "matgen_host staging", __FILE__, __LINE__);
+    for (int64_t c0 = 0; c0 < ncols && rc == CHPL_OK; c0 += per) {
+        const int64_t nc = std::min(per, ncols - c0);
+        rc = matgen(st, d, (size_t)N, (size_t)N, (size_t)nc, 0, c0, ncols, seed);
+        if (rc != CHPL_OK) break;
+        e = cudaMemcpy2DAsync(Ab + (size_t)c0 * ldab, ldab * sizeof(double), d, (size_t)N * sizeof(double),
+                              (size_t)N * sizeof(double), (size_t)nc, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = cuda_fail(e, "matgen_host copy", __FILE__, __LINE__);
+    }
+    if (d) cudaFree(d);
+    cudaStreamDestroy(st);
+    return rc;
 }
 
 extern "C" int chpl_matgen_cyclic(void* stream, double* A, size_t lda, int64_t N, int64_t NB, int P, int Q, int pr,
@@ -373,4 +431,11 @@ extern "C" int chpl_residual(void* stream, int64_t N, uint64_t seed, const doubl
 {
     if (!resid) { set_error("resid is NULL"); return CHPL_ERR_INVALID; }
     return residual((cudaStream_t)stream, N, seed, x, resid);
+}
+
+extern "C" int chpl_residual_matrix(void* stream, int64_t N, const double* Ab, size_t ldab, const double* x,
+                                    double* resid)
+{
+    if (!resid) { set_error("resid is NULL"); return CHPL_ERR_INVALID; }
+    return residual_matrix((cudaStream_t)stream, N, Ab, ldab, x, resid);
 }

@@ -50,6 +50,13 @@ namespace chpl {
         }                                                                          \
     } while (0)
 
+// CUDA call whose failure returns fin(status) (fin releases the caller's resources)
+#define CHPL_CUDA_OR(call, fin)                                                    \
+    do {                                                                           \
+        cudaError_t e_ = (call);                                                   \
+        if (e_ != cudaSuccess) return fin(::chpl::cuda_fail(e_, #call, __FILE__, __LINE__)); \
+    } while (0)
+
 enum Phase { PH_PANEL = 0, PH_LASWP, PH_TRSM, PH_SPLIT, PH_GEMM, PH_UPD_FP64, PH_SOLVE, PH_COMM, PH_N };
 
 namespace {
@@ -484,7 +491,28 @@ struct Solver {
 
 }  // namespace
 
-int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)
+namespace {
+
+struct Events {
+    cudaEvent_t e[4] = {nullptr, nullptr, nullptr, nullptr};
+    int create()
+    {
+        for (auto& x : e) CHPL_CUDA(cudaEventCreate(&x));
+        return CHPL_OK;
+    }
+    ~Events()
+    {
+        for (auto x : e)
+            if (x) cudaEventDestroy(x);
+    }
+};
+
+// One solve.  Ab == nullptr: the generated system (seed cfg->seed), verified
+// against the generator.  Otherwise [A | b] is copied in from host memory Ab
+// (leading dimension ldab) and, when verify, copied in again after the solve
+// to compute the residual against it.
+int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int verify, chpl_hpl_result* res,
+             double* x_out)
 {
     if (!cfg || !res) { set_error("cfg/res NULL"); return CHPL_ERR_INVALID; }
     std::memset(res, 0, sizeof(*res));
@@ -492,16 +520,30 @@ int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_o
     if (cfg->agg < 0 || (int64_t)cfg->agg * cfg->NB > 16384) { set_error("agg * NB must be <= 16384"); return CHPL_ERR_INVALID; }
     if (cfg->P != 1 || cfg->Q != 1) { set_error("chpl_hpl_run drives one GPU; use the grid driver for P x Q > 1"); return CHPL_ERR_INVALID; }
     if (cfg->emulate && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
+    if (Ab && (int64_t)ldab < cfg->N) { set_error("ldab < N"); return CHPL_ERR_INVALID; }
     Solver s;
     int rc = s.init(*cfg);
     if (rc != CHPL_OK) { s.destroy(); return rc; }
-    auto finish = [&](int code) { s.destroy(); return code; };
-
-    cudaEvent_t g0, g1, t0, t1;
-    cudaEventCreate(&g0); cudaEventCreate(&g1); cudaEventCreate(&t0); cudaEventCreate(&t1);
-    cudaEventRecord(g0, s.s0);
-    rc = matgen(s.s0, s.A, (size_t)s.ld, (size_t)s.N, (size_t)s.ncols, 0, 0, s.ncols, cfg->seed);
+    double* xs = nullptr;   // x kept aside while [A | b] is copied in again for the residual
+    auto finish = [&](int code) {
+        if (xs) cudaFree(xs);
+        s.destroy();
+        return code;
+    };
+    Events ev;
+    rc = ev.create();
     if (rc != CHPL_OK) return finish(rc);
+    cudaEvent_t g0 = ev.e[0], g1 = ev.e[1], t0 = ev.e[2], t1 = ev.e[3];
+    const size_t row_bytes = (size_t)s.N * sizeof(double);
+    cudaEventRecord(g0, s.s0);
+    if (Ab) {
+        cudaError_t e = cudaMemcpy2DAsync(s.A, (size_t)s.ld * sizeof(double), Ab, ldab * sizeof(double), row_bytes,
+                                          (size_t)s.ncols, cudaMemcpyHostToDevice, s.s0);
+        if (e != cudaSuccess) return finish(cuda_fail(e, "[A|b] host to device", __FILE__, __LINE__));
+    } else {
+        rc = matgen(s.s0, s.A, (size_t)s.ld, (size_t)s.N, (size_t)s.ncols, 0, 0, s.ncols, cfg->seed);
+        if (rc != CHPL_OK) return finish(rc);
+    }
     cudaEventRecord(g1, s.s0);
     cudaEventRecord(t0, s.s0);
     cudaStreamWaitEvent(s.sP, t0, 0);
@@ -529,17 +571,43 @@ int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_o
     res->n_emulated = s.n_emu;
     s.gemm_stats(res);
     // x = column N
-    double* dx = s.at(0, s.N);
-    rc = residual(s.s0, s.N, cfg->seed, dx, &res->resid);
-    if (rc != CHPL_OK) return finish(rc);
+    const double* dx = s.at(0, s.N);
+    if (!Ab) {
+        rc = residual(s.s0, s.N, cfg->seed, dx, &res->resid);
+        if (rc != CHPL_OK) return finish(rc);
+    } else if (verify) {
+        CHPL_CUDA_OR(cudaMalloc((void**)&xs, row_bytes), finish);
+        CHPL_CUDA_OR(cudaMemcpyAsync(xs, dx, row_bytes, cudaMemcpyDeviceToDevice, s.s0), finish);
+        CHPL_CUDA_OR(cudaMemcpy2DAsync(s.A, (size_t)s.ld * sizeof(double), Ab, ldab * sizeof(double), row_bytes,
+                                       (size_t)s.ncols, cudaMemcpyHostToDevice, s.s0), finish);
+        rc = residual_matrix(s.s0, s.N, s.A, (size_t)s.ld, xs, &res->resid);
+        if (rc != CHPL_OK) return finish(rc);
+        dx = xs;
+    } else {
+        res->resid = std::nan("");
+    }
     res->passed = (hinfo == 0) && std::isfinite(res->resid) && res->resid < cfg->threshold;
     if (x_out) {
-        e = cudaMemcpy(x_out, dx, (size_t)s.N * sizeof(double), cudaMemcpyDeviceToHost);
+        e = cudaMemcpyAsync(x_out, dx, row_bytes, cudaMemcpyDeviceToHost, s.s0);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s.s0);
         if (e != cudaSuccess) return finish(cuda_fail(e, "x readback", __FILE__, __LINE__));
     }
-    cudaEventDestroy(g0); cudaEventDestroy(g1); cudaEventDestroy(t0); cudaEventDestroy(t1);
     if (hinfo != 0) { set_error("exact zero pivot at column %d", hinfo); return finish(CHPL_ERR_SINGULAR); }
     return finish(CHPL_OK);
+}
+
+}  // namespace
+
+int hpl_single_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)
+{
+    return run_impl(cfg, nullptr, 0, 1, res, x_out);
+}
+
+int hpl_single_run_host(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int verify, chpl_hpl_result* res,
+                        double* x_out)
+{
+    if (!Ab) { set_error("Ab is NULL"); return CHPL_ERR_INVALID; }
+    return run_impl(cfg, Ab, ldab, verify, res, x_out);
 }
 
 }  // namespace chpl
@@ -567,4 +635,10 @@ extern "C" void chpl_hpl_default_config(chpl_hpl_config* cfg)
 extern "C" int chpl_hpl_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)
 {
     return chpl::hpl_single_run(cfg, res, x_out);
+}
+
+extern "C" int chpl_hpl_run_host(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int verify,
+                                 chpl_hpl_result* res, double* x_out)
+{
+    return chpl::hpl_single_run_host(cfg, Ab, ldab, verify, res, x_out);
 }

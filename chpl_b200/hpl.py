@@ -167,11 +167,79 @@ def run(cfg: Config, want_x: bool = False) -> Result:
     x = np.empty(cfg.N, dtype=np.float64) if want_x else None
     xp = x.ctypes.data if want_x else None
     _lib.check(L.chpl_hpl_run(ctypes.byref(c), ctypes.byref(r), xp), "chpl_hpl_run")
+    return _result(cfg, r, x)
+
+
+def _result(cfg: Config, r, x) -> Result:
     return Result(N=cfg.N, NB=cfg.NB, P=cfg.P, Q=cfg.Q, time_s=r.time_s, tflops=r.tflops, resid=r.resid,
                   passed=bool(r.passed), threshold=cfg.threshold, matgen_s=r.matgen_s,
                   phases={p: r.phase_s[i] for i, p in enumerate(PHASES)}, n_emulated=r.n_emulated,
                   n_launches=r.n_launches, gemm_launches=r.gemm_launches, gemm_kernel_s=r.gemm_kernel_s,
                   gemm_int8_ops=r.gemm_int8_ops, gemm_fp64eq_flops=r.gemm_fp64eq_flops, x=x)
+
+
+class HostSystem:
+    """[A | b] (N x (N+1), column-major) in page-locked host memory
+    (chpl_host_alloc); ``array`` is a numpy view of shape (N+1, N): row j of
+    the view is column j of the system."""
+
+    def __init__(self, N: int):
+        L = _lib.load()
+        self.N = N
+        self.ld = N
+        self.nbytes = N * (N + 1) * 8
+        p = ctypes.c_void_p()
+        _lib.check(L.chpl_host_alloc(self.nbytes, ctypes.byref(p)), "chpl_host_alloc")
+        self.ptr = p.value
+        buf = (ctypes.c_double * (N * (N + 1))).from_address(self.ptr)
+        self.array = np.frombuffer(buf, dtype=np.float64).reshape(N + 1, N)
+
+    def generate(self, seed: int = 42) -> None:
+        """The generated system of ``run`` (same elements), produced on the device."""
+        _lib.check(_lib.load().chpl_matgen_host(self.N, seed, self.ptr, self.ld), "chpl_matgen_host")
+
+    def close(self) -> None:
+        if self.ptr:
+            self.array = None
+            _lib.load().chpl_host_free(self.ptr)
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+def run_host(cfg: Config, Ab, ldab: int | None = None, verify: bool = True, want_x: bool = True) -> Result:
+    """One solve of a caller-supplied system read from host memory (P = Q = 1).
+
+    ``Ab`` is a HostSystem, a numpy array holding [A | b] column-major (shape
+    (N+1, ldab) C-contiguous, or (ldab, N+1) Fortran-ordered), or a raw host
+    address with ``ldab`` given.  ``cfg.seed`` is not used."""
+    L = _lib.load()
+    if isinstance(Ab, HostSystem):
+        ptr, ld = Ab.ptr, Ab.ld
+    elif isinstance(Ab, np.ndarray):
+        if Ab.dtype != np.float64:
+            raise TypeError("Ab must be float64")
+        if Ab.flags.c_contiguous and Ab.shape[0] == cfg.N + 1:
+            ld = Ab.shape[1]
+        elif Ab.flags.f_contiguous and Ab.ndim == 2 and Ab.shape[1] == cfg.N + 1:
+            ld = Ab.shape[0]
+        else:
+            raise ValueError("Ab must hold the N+1 columns of [A | b] contiguously, column-major")
+        ptr = Ab.ctypes.data
+    else:
+        if ldab is None:
+            raise ValueError("ldab is required with a raw address")
+        ptr, ld = int(Ab), ldab
+    c = cfg.to_c()
+    r = _lib.HplResult()
+    x = np.empty(cfg.N, dtype=np.float64) if want_x else None
+    _lib.check(L.chpl_hpl_run_host(ctypes.byref(c), ptr, ld if ldab is None else ldab, int(verify), ctypes.byref(r),
+                                   x.ctypes.data if want_x else None), "chpl_hpl_run_host")
+    return _result(cfg, r, x)
 
 
 def format_single(res: Result, cfg: Config) -> str:

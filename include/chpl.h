@@ -41,6 +41,12 @@ const char *chpl_version(void);
 /* Sticky device-side error (timeouts inside kernels) of the current device:
  * writes it to *status and clears it.  Synchronizes the device. */
 int chpl_device_status(int *status);
+/* Page-locked (pinned) host memory, portable across devices: host buffers of
+ * chpl_hpl_run_host / chpl_matgen_host in it copy at the link's full
+ * bandwidth.  No reference counterpart (the reference keeps every matrix on
+ * the device). */
+int chpl_host_alloc(size_t bytes, void **ptr);
+int chpl_host_free(void *ptr);
 
 /* ------------------------------------------------------------------------ */
 /* Ozaki scheme II emulated DGEMM (trailing-matrix update)                   */
@@ -150,6 +156,12 @@ int chpl_matgen(void *stream, double *A, size_t lda, size_t m, size_t n, int64_t
  * (pr, qc) of a P x Q grid with block NB (src/chpl_p2.cu:615-626,951-957). */
 int chpl_matgen_cyclic(void *stream, double *A, size_t lda, int64_t N, int64_t NB, int P, int Q, int pr,
                        int qc, uint64_t seed);
+/* The generated N x (N+1) system [A | b] written into HOST memory Ab
+ * (column-major, ldab >= N): generated on the current device in column blocks
+ * of <= 256 MiB (the same elements as chpl_matgen) and copied out.
+ * Synchronous.  Input preparation for chpl_hpl_run_host; the reference has
+ * no host copy of the matrix (matgen2d_kernel, src/chpl_p2.cu:76-87). */
+int chpl_matgen_host(int64_t N, uint64_t seed, double *Ab, size_t ldab);
 
 /*
  * Row interchanges, LAPACK dlaswp semantics on columns [0, ncols) of A:
@@ -181,6 +193,12 @@ int chpl_panel_getrf_f64(void *stream, int64_t m, int64_t n, double *A, size_t l
  * src/chpl_p2.cu:1886-1932.
  */
 int chpl_residual(void *stream, int64_t N, uint64_t seed, const double *x, double *resid);
+/* The same residual for a system held in device memory: Ab is [A | b]
+ * (N x (N+1), column-major, ldab >= N, b = column N).  Same reduction order
+ * as chpl_residual, so a generated system gives the identical value.
+ * Synchronizes.  Replaces the same verification
+ * (src/chpl_single.cu:762-817) for systems that are not generated. */
+int chpl_residual_matrix(void *stream, int64_t N, const double *Ab, size_t ldab, const double *x, double *resid);
 
 /*
  * Failure-detection self-test (no reference counterpart): one bounded
@@ -241,6 +259,23 @@ void chpl_hpl_default_config(chpl_hpl_config *cfg);
  * chpl_single (src/chpl_single.cu:733-840).
  */
 int chpl_hpl_run(const chpl_hpl_config *cfg, chpl_hpl_result *res, double *x_out);
+
+/*
+ * One solve of a caller-supplied system from HOST memory on the current
+ * device (P = Q = 1): [A | b] (N x (N+1), column-major, ldab >= N, b = column
+ * N) is copied to the device (page-locked memory from chpl_host_alloc copies
+ * at full bandwidth; pageable memory works, slower), factored and solved with
+ * the same kernels and schedule as chpl_hpl_run (cfg->seed is unused), and x
+ * is written to x_out (host, N doubles; may be NULL).  verify = 1 copies
+ * [A | b] in again after the solve and computes the HPL scaled residual
+ * against it (res->resid, res->passed); verify = 0 leaves res->resid NaN and
+ * res->passed 0.  res->time_s is factor + solve (device time), res->matgen_s
+ * the host-to-device copy of [A | b].  The host-buffer form of run_case
+ * (src/chpl_single.cu:733-840), whose input the reference always generates
+ * on the device (src/chpl_single.cu:750).
+ */
+int chpl_hpl_run_host(const chpl_hpl_config *cfg, const double *Ab, size_t ldab, int verify,
+                      chpl_hpl_result *res, double *x_out);
 
 /* ------------------------------------------------------------------------ */
 /* P x Q process grid (one process per GPU, NCCL over NVLink)                */

@@ -82,3 +82,23 @@ def test_invalid_config_rejected_without_gpu():
     r = _lib.HplResult()
     assert L.chpl_hpl_run(ctypes.byref(c), ctypes.byref(r), None) == _lib.CHPL_ERR_INVALID
     assert b"N" in L.chpl_last_error_string()
+
+
+def test_host_entry_points_reject_bad_arguments_without_gpu():
+    """Argument checks of the host-buffer entry points run before any CUDA call."""
+    L = _lib.load()
+    c = _lib.HplConfig()
+    L.chpl_hpl_default_config(ctypes.byref(c))
+    c.N = 100
+    r = _lib.HplResult()
+    assert L.chpl_hpl_run_host(ctypes.byref(c), None, 100, 1, ctypes.byref(r), None) == _lib.CHPL_ERR_INVALID
+    buf = (ctypes.c_double * 16)()
+    assert L.chpl_hpl_run_host(ctypes.byref(c), buf, 99, 1, ctypes.byref(r), None) == _lib.CHPL_ERR_INVALID
+    assert b"ldab" in L.chpl_last_error_string()
+    assert L.chpl_matgen_host(0, 42, buf, 1) == _lib.CHPL_ERR_INVALID
+    assert L.chpl_matgen_host(10, 42, buf, 9) == _lib.CHPL_ERR_INVALID
+    p = ctypes.c_void_p()
+    assert L.chpl_host_alloc(0, ctypes.byref(p)) == _lib.CHPL_ERR_INVALID
+    assert L.chpl_host_free(None) == _lib.CHPL_OK
+    res = ctypes.c_double()
+    assert L.chpl_residual_matrix(None, 10, None, 10, None, ctypes.byref(res)) == _lib.CHPL_ERR_INVALID

@@ -181,3 +181,82 @@ def test_hpl_emulated_vs_oracle_small(cuda):
     x, _, _ = oracle.hpl_solve(N, NB, L=12)
     assert np.allclose(res.x, x, rtol=1e-6, atol=1e-8)
     assert res.passed
+
+
+# ---------------------------------------------------------------- host-buffer solves (chpl_hpl_run_host)
+@pytest.mark.parametrize("N,pad", [(700, 0), (6000, 0), (513, 9)])
+def test_matgen_host_bitexact(cuda, N, pad):
+    """chpl_matgen_host writes the generated system into host memory; N = 6000
+    spans two 256 MiB column blocks, pad > 0 a leading dimension above N."""
+    L = _lib.load()
+    ld = N + pad
+    buf = np.full((N + 1, ld), 7.0)
+    _lib.check(L.chpl_matgen_host(N, 42, buf.ctypes.data, ld), "chpl_matgen_host")
+    assert np.array_equal(buf[:, :N].T, oracle.hpl_system_fast(N))
+    assert np.all(buf[:, N:] == 7.0)
+
+
+def test_residual_matrix_equals_generated_residual(cuda):
+    """Same reduction order: the residual of a device copy of [A|b] equals the
+    residual computed by regenerating it, bit for bit."""
+    L = _lib.load()
+    N, ld = 1000, 1024
+    d = torch.zeros((N + 1, ld), dtype=torch.float64, device="cuda")
+    _lib.check(L.chpl_matgen(0, d.data_ptr(), ld, N, N + 1, 0, 0, N + 1, 42), "chpl_matgen")
+    S = oracle.hpl_system(N)
+    x = np.linalg.solve(S[:, :N], S[:, N]) * (1 + 1e-9)
+    dx = torch.from_numpy(x).cuda()
+    r1, r2 = ctypes.c_double(), ctypes.c_double()
+    _lib.check(L.chpl_residual(0, N, 42, dx.data_ptr(), ctypes.byref(r1)), "chpl_residual")
+    _lib.check(L.chpl_residual_matrix(0, N, d.data_ptr(), ld, dx.data_ptr(), ctypes.byref(r2)), "residual_matrix")
+    assert r1.value == r2.value
+
+
+def test_run_host_equals_generated_run(cuda):
+    """The generated system passed through host memory gives the same x and
+    residual as chpl_hpl_run generating it on the device."""
+    cfg = hpl.Config(N=4096, NB=256, moduli=11)
+    a = hpl.run(cfg, want_x=True)
+    with hpl.HostSystem(cfg.N) as S:
+        S.generate(cfg.seed)
+        b = hpl.run_host(cfg, S, verify=True)
+        c = hpl.run_host(cfg, S, verify=False)
+    assert a.passed and b.passed
+    assert np.array_equal(a.x, b.x) and np.array_equal(a.x, c.x)
+    assert a.resid == b.resid
+    assert np.isnan(c.resid) and not c.passed
+    assert b.matgen_s > 0.0 and b.time_s > 0.0
+
+
+@pytest.mark.parametrize("emulate", [True, False])
+def test_run_host_arbitrary_system(cuda, emulate):
+    """A system that is not the generated one (pageable numpy memory, ld > N):
+    x against LAPACK, the residual against the oracle's formula."""
+    N, ld = 3000, 3003
+    rng = np.random.default_rng(7)
+    Ab = np.zeros((N + 1, ld))          # column j of [A|b] is row j
+    Ab[:, :N] = rng.uniform(-0.5, 0.5, (N + 1, N))
+    res = hpl.run_host(hpl.Config(N=N, NB=256, moduli=12, emulate=emulate), Ab, verify=True)
+    A = Ab[:, :N].T
+    xs = scipy.linalg.solve(A[:, :N], A[:, N])
+    assert res.passed, res.resid
+    assert np.allclose(res.x, xs, rtol=1e-7, atol=1e-9)
+    # ||Ax - b|| is a difference of rounded sums: orders of summation differ
+    assert res.resid == pytest.approx(oracle.hpl_residual_from(A, res.x), rel=1e-3)
+
+
+def test_run_host_detects_a_wrong_solution(cuda):
+    """The residual is computed against the system supplied: once b is changed,
+    the x solved before fails the check."""
+    N = 1200
+    rng = np.random.default_rng(3)
+    Ab = rng.uniform(-0.5, 0.5, (N + 1, N))
+    good = hpl.run_host(hpl.Config(N=N, NB=128, emulate=False), Ab, verify=True)
+    assert good.passed
+    L = _lib.load()
+    dAb = torch.from_numpy(Ab.copy()).cuda()
+    dAb[N, 0] += 1.0                     # b_0 changed
+    dx = torch.from_numpy(good.x).cuda()
+    r = ctypes.c_double()
+    _lib.check(L.chpl_residual_matrix(0, N, dAb.data_ptr(), N, dx.data_ptr(), ctypes.byref(r)), "residual_matrix")
+    assert r.value > 16.0

@@ -2,6 +2,7 @@
 
     python -m chpl_b200.cases gemm --m 32768 --n 32768 --k 4096 --moduli 11 [--reps 3]
     python -m chpl_b200.cases hpl --N 65536 --NB 1024 [--no-lookahead]
+    python -m chpl_b200.cases laswp --rows 139264 --cols 65536 --swaps 1024
 
 Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (BASELINE
 config 2) generated on the device.
@@ -81,6 +82,40 @@ def panel_case(m: int, n: int, reps: int) -> dict:
     return {"case": "panel", "m": m, "n": n, "ms": best * 1e3, "fp64_tflops": fl / best / 1e12, "info": int(info.item())}
 
 
+def laswp_case(rows: int, cols: int, swaps: int, reps: int) -> dict:
+    """Interchanges of `swaps` partial-pivoting rows (ipiv[i] uniform in [i, rows))
+    on a rows x cols column-major matrix: plan + apply, as the solver's
+    trailing-column interchanges.  Algorithmic bytes: 16 per moved element."""
+    import ctypes
+
+    import numpy as np
+
+    from . import _lib
+    L = _lib.load()
+    rng = np.random.default_rng(1)
+    ipiv = np.array([rng.integers(i, rows) for i in range(swaps)], dtype=np.int64)
+    perm = np.arange(rows)
+    for i, p in enumerate(ipiv):
+        perm[i], perm[p] = perm[p], perm[i]
+    moved = int(np.count_nonzero(perm != np.arange(rows)))
+    A = torch.empty(cols, rows, dtype=torch.float64, device="cuda")
+    A.copy_(torch.rand(cols, rows, dtype=torch.float64, device="cuda"))
+    dpiv = torch.from_numpy(ipiv).cuda()
+    work = torch.empty(L.chpl_laswp_work_bytes(rows, swaps), dtype=torch.uint8, device="cuda")
+    best = 1e30
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _lib.check(L.chpl_laswp(0, A.data_ptr(), rows, cols, 0, swaps, dpiv.data_ptr(), rows, work.data_ptr()),
+                   "chpl_laswp")
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e-3)
+    gb = 16.0 * moved * cols / 1e9
+    return {"case": "laswp", "rows": rows, "cols": cols, "swaps": swaps, "moved_rows": moved, "ms": best * 1e3,
+            "algorithmic_gb": gb, "gbs": gb / best}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -96,6 +131,11 @@ def main() -> None:
     pn.add_argument("--m", type=int, default=65536)
     pn.add_argument("--n", type=int, default=1024)
     pn.add_argument("--reps", type=int, default=3)
+    lw = sub.add_parser("laswp")
+    lw.add_argument("--rows", type=int, default=139264)
+    lw.add_argument("--cols", type=int, default=65536)
+    lw.add_argument("--swaps", type=int, default=1024)
+    lw.add_argument("--reps", type=int, default=5)
     h = sub.add_parser("hpl")
     h.add_argument("--N", type=int, default=16384)
     h.add_argument("--NB", type=int, default=1024)
@@ -113,6 +153,8 @@ def main() -> None:
         print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled, a.sustain)), flush=True)
     elif a.what == "panel":
         print(json.dumps(panel_case(a.m, a.n, a.reps)), flush=True)
+    elif a.what == "laswp":
+        print(json.dumps(laswp_case(a.rows, a.cols, a.swaps, a.reps)), flush=True)
     else:
         r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=a.lookahead and not a.no_lookahead,
                                emulate=not a.fp64, agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve,

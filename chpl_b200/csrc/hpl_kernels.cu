@@ -144,27 +144,42 @@ __global__ void __launch_bounds__(1024) laswp_plan_kernel(const int64_t* __restr
 }
 
 // Apply the planned permutation to columns [c0, c0+ncols) of A.  Each CTA owns
-// kLaswpCols columns: it reads every source row of its columns into shared
-// memory, then writes every destination row, so in-place is safe.
-constexpr int kLaswpCols = 4;
-
-__global__ void __launch_bounds__(256) laswp_apply_kernel(double* __restrict__ A, long long lda, long long ncols,
-                                                          const int* __restrict__ dst, const int* __restrict__ src,
-                                                          const int* __restrict__ cnt)
+// a few whole columns: it reads every source row of its columns, then (after a
+// barrier) writes every destination row, so in-place is safe.  The moved rows
+// of a column are scattered over ~N rows of a column-major matrix, so each
+// access is its own DRAM sector; what bounds the kernel is how many of them
+// are in flight.  The register form gives each thread PPT pairs x COLS columns
+// of independent loads (up to 32) before the barrier.
+template <int PPT, int COLS>
+__global__ void __launch_bounds__(256) laswp_apply_reg_kernel(double* __restrict__ A, long long lda, long long ncols,
+                                                              const int* __restrict__ dst, const int* __restrict__ src,
+                                                              const int* __restrict__ cnt)
 {
-    extern __shared__ double buf[];  // [cnt][kLaswpCols]
     const int np = cnt[0];
-    const long long c0 = (long long)blockIdx.x * kLaswpCols;
-    const int nc = (int)min((long long)kLaswpCols, ncols - c0);
-    if (np == 0 || nc <= 0) return;
-    for (int c = 0; c < nc; ++c) {
+    const long long c0 = (long long)blockIdx.x * COLS;
+    if (np == 0 || c0 >= ncols) return;
+    const int nc = (int)min((long long)COLS, ncols - c0);
+    int s[PPT], d[PPT];
+#pragma unroll
+    for (int j = 0; j < PPT; ++j) {
+        const int t = threadIdx.x + j * 256;
+        s[j] = t < np ? src[t] : -1;
+        d[j] = t < np ? dst[t] : -1;
+    }
+    double v[COLS][PPT];
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
         const double* col = A + (c0 + c) * lda;
-        for (int t = threadIdx.x; t < np; t += blockDim.x) buf[t * kLaswpCols + c] = col[src[t]];
+#pragma unroll
+        for (int j = 0; j < PPT; ++j) v[c][j] = (c < nc && s[j] >= 0) ? col[s[j]] : 0.0;
     }
     __syncthreads();
-    for (int c = 0; c < nc; ++c) {
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
         double* col = A + (c0 + c) * lda;
-        for (int t = threadIdx.x; t < np; t += blockDim.x) col[dst[t]] = buf[t * kLaswpCols + c];
+#pragma unroll
+        for (int j = 0; j < PPT; ++j)
+            if (c < nc && d[j] >= 0) col[d[j]] = v[c][j];
     }
 }
 
@@ -184,20 +199,34 @@ int laswp_plan(cudaStream_t st, const int64_t* ipiv, int64_t k1, int64_t k2, voi
     return CHPL_OK;
 }
 
+template <int PPT, int COLS>
+static int launch_apply_reg(cudaStream_t st, double* A, size_t lda, int64_t ncols, const int* dst, const int* src,
+                            const int* cnt)
+{
+    const long long nb = (ncols + COLS - 1) / COLS;
+    if (nb > 0x7fffffffLL) { set_error("laswp: too many columns"); return CHPL_ERR_UNSUPPORTED; }
+    laswp_apply_reg_kernel<PPT, COLS><<<(unsigned)nb, 256, 0, st>>>(A, (long long)lda, (long long)ncols, dst, src, cnt);
+    CHPL_CUDA(cudaGetLastError());
+    return CHPL_OK;
+}
+
 int laswp_apply(cudaStream_t st, double* A, size_t lda, int64_t c0, int64_t ncols, int64_t nswaps, const void* work)
 {
     if (ncols <= 0 || nswaps <= 0) return CHPL_OK;
     const int* cnt = static_cast<const int*>(work);
     const int* dst = cnt + 16;
     const int* src = dst + 2 * nswaps;
-    const size_t smem = (size_t)(2 * nswaps) * kLaswpCols * sizeof(double);
-    if (smem > 48 * 1024) CHPL_CUDA(cudaFuncSetAttribute(laswp_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const long long nb = (ncols + kLaswpCols - 1) / kLaswpCols;
-    if (nb > 0x7fffffffLL) { set_error("laswp: too many columns"); return CHPL_ERR_UNSUPPORTED; }
-    laswp_apply_kernel<<<(unsigned)nb, 256, smem, st>>>(A + (size_t)c0 * lda, (long long)lda, (long long)ncols, dst, src,
-                                                         cnt);
-    CHPL_CUDA(cudaGetLastError());
-    return CHPL_OK;
+    double* Ac = A + (size_t)c0 * lda;
+    // the plan moves at most 2 * nswaps rows; pick the register form that holds them
+    const int64_t maxpairs = 2 * nswaps;
+    if (maxpairs <= 256) return launch_apply_reg<1, 8>(st, Ac, lda, ncols, dst, src, cnt);
+    if (maxpairs <= 512) return launch_apply_reg<2, 8>(st, Ac, lda, ncols, dst, src, cnt);
+    if (maxpairs <= 1024) return launch_apply_reg<4, 8>(st, Ac, lda, ncols, dst, src, cnt);
+    if (maxpairs <= 2048) return launch_apply_reg<8, 4>(st, Ac, lda, ncols, dst, src, cnt);
+    static_assert(2 * kLaswpMaxSwaps <= 16 * 256, "a plan's pairs must fit the widest register form");
+    if (maxpairs <= 4096) return launch_apply_reg<16, 2>(st, Ac, lda, ncols, dst, src, cnt);
+    set_error("laswp: at most %d interchanges per plan", kLaswpMaxSwaps);
+    return CHPL_ERR_UNSUPPORTED;
 }
 
 // ipiv_abs[base + i] = base + rel[i] - 1 (1-based relative -> 0-based absolute)

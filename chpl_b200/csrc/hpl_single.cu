@@ -92,6 +92,21 @@ struct PhaseTimer {
     }
 };
 
+// Panels per super-block when the caller leaves it to the library (agg = 0).
+// Aggregating panels into updates of depth k = 4096 runs the GEMM at its best
+// rate, but each emulated update carries an error that grows with sqrt(k), and
+// the aggregated form also computes U12 as inv(L) * A12 through the emulated
+// GEMM.  The HPL residual divides by eps * N * ||A|| ||x||, which outgrows that
+// error only at large N: at 11 moduli the aggregated solve measured residuals
+// 23.7 (N = 16384, a failure), 9.1 (32768), 4.8 (65536) and 2.3 (139264),
+// while N = 16384 without aggregation (k = NB = 1024) gave 3.9 in the same
+// time.  Below N = 65536 the panel dominates anyway, so nothing is aggregated.
+constexpr int64_t kAggMinN = 65536;
+static int auto_agg(int64_t N, int64_t NB)
+{
+    return N >= kAggMinN ? (int)std::max<int64_t>(1, 4096 / NB) : 1;
+}
+
 struct Solver {
     chpl_hpl_config cfg{};
     int64_t N = 0, NB = 0, K = 0, ld = 0, ncols = 0;
@@ -142,7 +157,7 @@ struct Solver {
         cfg = c;
         N = c.N;
         NB = std::min<int64_t>(c.NB, N);
-        agg = c.agg > 0 ? c.agg : (int)std::max<int64_t>(1, 4096 / NB);
+        agg = c.agg > 0 ? c.agg : auto_agg(N, NB);
         K = std::min<int64_t>(agg * NB, N);
         ld = (int64_t)round_up((size_t)N, 32);
         ncols = N + 1;

@@ -105,7 +105,9 @@ class Config:
 def single_config_from_env(N: int, env=None) -> Config:
     """chpl_single's configuration (src/chpl_single.cu:842-869, launcher defaults
     scripts/mpirun_chpl:71-76).  HPLS_AGG groups panels into super-blocks whose
-    trailing update runs with k = AGG * NB (0 = automatic, k = 4096)."""
+    trailing update runs with k = AGG * NB (0 = automatic: k = 4096 from
+    N = 65536 up, k = NB below, where deeper emulated updates cost residual
+    margin)."""
     env = os.environ if env is None else env
     backend = env.get("HPLS_BACKEND", "gemmul8")
     if backend not in ("native", "gemmul8", "ozaki"):

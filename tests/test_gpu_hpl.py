@@ -148,6 +148,14 @@ def test_hpl_emulated_passes(cuda, L):
     assert res.n_emulated > 0
 
 
+def test_hpl_config1_passes_at_11_moduli(cuda):
+    """BASELINE config 1 (N = 16384, NB = 1024, 11 moduli) with the library's
+    default aggregation passes the HPL check with margin (the aggregated
+    k = 4096 form gave 23.7 here, a failure)."""
+    res = hpl.run(hpl.Config(N=16384, NB=1024, moduli=11), want_x=False)
+    assert res.passed and res.resid < 8.0, res.resid
+
+
 def test_hpl_lookahead_is_deterministic(cuda):
     """Lookahead only reorders independent work: x is bit-identical to the
     serial schedule, and reruns are bit-identical (src/chpl_p2.cu residuals are
@@ -241,8 +249,9 @@ def test_run_host_arbitrary_system(cuda, emulate):
     xs = scipy.linalg.solve(A[:, :N], A[:, N])
     assert res.passed, res.resid
     assert np.allclose(res.x, xs, rtol=1e-7, atol=1e-9)
-    # ||Ax - b|| is a difference of rounded sums: orders of summation differ
-    assert res.resid == pytest.approx(oracle.hpl_residual_from(A, res.x), rel=1e-3)
+    # ||Ax - b|| is a difference of rounded sums whose order differs between
+    # the two, and near the rounding floor (the FP64 solve) that is most of it
+    assert res.resid == pytest.approx(oracle.hpl_residual_from(A, res.x), rel=0.05, abs=0.01)
 
 
 def test_run_host_detects_a_wrong_solution(cuda):

@@ -71,3 +71,29 @@ def test_report_formats():
     assert "WC2" in s and "PASSED" in s and "1000" in s
     s = hpl.format_single(r, hpl.Config(N=1000, NB=128))
     assert "HPLS_gemmul8" in s and "PASSED" in s
+
+
+def test_bench_e2e_order_follows_host_memory(monkeypatch):
+    """The host-buffer leg runs at the bench's N when the pinned [A|b] fits in
+    host memory with a margin, at the largest multiple of NB that fits
+    otherwise, and not at all below N = 16384."""
+    import bench
+    GiB = 1 << 30
+    need = 139264 * 139265 * 8
+    monkeypatch.setattr(bench, "host_memory_available", lambda: need + 40 * GiB)
+    assert bench.e2e_order(139264, 1024) == (139264, None)
+    monkeypatch.setattr(bench, "host_memory_available", lambda: 62 * GiB)
+    n, why = bench.e2e_order(139264, 1024)
+    assert n % 1024 == 0 and 16384 <= n < 139264 and n * (n + 1) * 8 <= (62 - 16) * GiB / 1.05
+    assert "pinned host memory" in why
+    monkeypatch.setattr(bench, "host_memory_available", lambda: 17 * GiB)
+    assert bench.e2e_order(139264, 1024)[0] is None
+    monkeypatch.setattr(bench, "host_memory_available", lambda: None)
+    assert bench.e2e_order(139264, 1024) == (None, "host memory size unknown")
+
+
+def test_bench_host_memory_reads_meminfo():
+    import bench
+    v = bench.host_memory_available()
+    assert v is None or v > 0
+

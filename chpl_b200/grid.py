@@ -165,9 +165,12 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
                                         "in this run (the sustained figure, for a kernel timed inside long solves)",
                          "peak_burst": peak_burst,
                          "launches": nl, "avg_launch_ms": gk / nl * 1e3 if nl else None},
-            "e2e": {"value": a.steps * flops(N) / wall / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": 80,
-                    "d2h_bytes_per_step": N * 8,
-                    "note": "public API chpl_grid_run per step (wall clock, max over ranks)"},
+            "e2e": {"value": a.steps * flops(N) / wall / 1e12, "unit": "TFLOPS",
+                    "h2d_bytes_per_step": ctypes.sizeof(_lib.HplConfig),
+                    "d2h_bytes_per_step": N * 8 + ctypes.sizeof(_lib.HplResult),
+                    "note": "public API chpl_grid_run per step (wall clock, max over ranks): on-device "
+                            "block-cyclic generation of the HPL system, solve, verification, x to the host; "
+                            "no host copy of the ranks' local pieces (~144 GB each) is made"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

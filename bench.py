@@ -370,6 +370,7 @@ def run_single(a) -> None:
             "launches": nl, "avg_launch_ms": gk / nl * 1e3 if nl else None,
             "fp64eq_tflops_in_kernel": sum(r.gemm_fp64eq_flops for r in res) / gk / 1e12 if gk else None}
     phases = {p: sum(r.phases[p] for r in res) / a.steps for p in hpl.PHASES}
+    outside = (solve - gk) / a.steps    # per step: everything the solve did outside the int8 GEMM kernel
     out = {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": solve / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -382,6 +383,7 @@ def run_single(a) -> None:
                    "timed_region": "factor + back substitution per step (device events); generation excluded"},
         "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
         "phases_s": phases,
+        "outside_gemm_s_per_step": outside,
         "roofline": roof,
         "e2e": None,
         "gpu_launches": sum(r.n_launches for r in res),

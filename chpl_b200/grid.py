@@ -138,6 +138,11 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
     nl = sum(r.gemm_launches for r in res)
     launches = sum(r.n_launches for r in res)
     phases = {p: max_over_ranks(sum(r.phases[p] for r in res) / a.steps) for p in hpl.PHASES}
+    # time each rank's solve spent outside its int8 GEMM kernel (panel, exchanges, waits for
+    # other ranks, interchanges, splits): the largest and smallest over ranks, per step
+    outside = (sum(r.time_s for r in res) - gk) / a.steps
+    outside_max = max_over_ranks(outside)
+    outside_min = -max_over_ranks(-outside)
     tpu = traffic_per_unit() if traffic_per_unit else None
     # the cuBLAS int8 denominator, measured after the solves (whose memory plan wants every free byte),
     # by every rank on its own GPU
@@ -156,6 +161,8 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
                        "timed_region": "factor + back substitution (device events, max over ranks)"},
             "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
             "phases_s_max_over_ranks": phases,
+            "outside_gemm_s_per_step": {"max_over_ranks": outside_max, "min_over_ranks": outside_min,
+                                        "note": "solve time minus the rank's own int8 GEMM kernel time"},
             "roofline": {"bound": "tensor", "achieved": ops / gk / 1e12 if gk else None, "peak": peak,
                          "unit": "TOPS (int8)",
                          "frac": (ops / gk / 1e12 / peak) if (gk and peak) else None,

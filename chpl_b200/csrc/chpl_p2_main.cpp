@@ -7,8 +7,11 @@
 // 16.0 when the file is missing or shorter than 13 lines (570-584);
 // CHPL2D_G8 (must be 1: the emulated update), CHPL2D_G8_MODULI (11),
 // CHPL2D_G8_FAST, CHPL2D_G8_NT (column chunk of the update) (685-691).
-// The grid is P x Q with P = 2 when the rank count is even (the reference's
-// fixed P = 2) and rank = P*qc + pr (528); one rank runs 1 x 1.
+// The grid is P x Q with rank = P*qc + pr (528): HPL.dat's P and Q (lines 11
+// and 12) when they multiply to the rank count with P <= 2, otherwise P = 2
+// for an even rank count (the reference's fixed P = 2); one rank runs 1 x 1.
+// CHPL_P2_DRY_RUN=1 prints the configuration and exits before any GPU or
+// network work.
 //
 // There is no MPI: rank, rank count and local rank come from the launcher's
 // environment (RANK / WORLD_SIZE / LOCAL_RANK as torchrun sets them, or
@@ -134,6 +137,7 @@ bool fetch_id(const char* host, int port, unsigned char* id, size_t len, double 
 struct Dat {
     int64_t N = 16384, NB = 1024;
     double thresh = 16.0;
+    int P = 0, Q = 0;  // lines 11 / 12, 0 when absent
 };
 
 Dat read_dat(const char* path)
@@ -150,6 +154,8 @@ Dat read_dat(const char* path)
         d.N = std::atoll(L[5].c_str());
         d.NB = std::atoll(L[7].c_str());
         d.thresh = std::atof(L[12].c_str());
+        d.P = std::atoi(L[10].c_str());
+        d.Q = std::atoi(L[11].c_str());
     }
     return d;
 }
@@ -166,8 +172,9 @@ int main(int argc, char** argv)
         if (rank == 0) std::fprintf(stderr, "chpl_p2 runs on 1 rank or an even number of ranks (got %d)\n", size);
         return 1;
     }
-    const int P = size > 1 ? 2 : 1, Q = size / P;
     const Dat dat = read_dat(argc > 1 ? argv[1] : nullptr);
+    const bool dat_grid = dat.P >= 1 && dat.P <= 2 && dat.Q >= 1 && dat.P * dat.Q == size;
+    const int P = dat_grid ? dat.P : (size > 1 ? 2 : 1), Q = size / P;
     chpl_hpl_config cfg;
     chpl_hpl_default_config(&cfg);
     cfg.N = dat.N;
@@ -186,6 +193,13 @@ int main(int argc, char** argv)
     if (!cfg.emulate && size > 1) {
         if (rank == 0) std::fprintf(stderr, "[chpl_p2] the grid runs the emulated update only (CHPL2D_G8=1)\n");
         return 1;
+    }
+    static const char* kDry[] = {"CHPL_P2_DRY_RUN", nullptr};
+    if (env_int(kDry, 0)) {
+        if (rank == 0)
+            std::printf("[chpl_p2] grid %dx%d N=%" PRId64 " NB=%" PRId64 " threshold=%g moduli=%d ranks=%d\n", P, Q,
+                        cfg.N, cfg.NB, cfg.threshold, cfg.moduli, size);
+        return 0;
     }
 
     static const char* kTimeout[] = {"CHPL_BOOTSTRAP_TIMEOUT", nullptr};

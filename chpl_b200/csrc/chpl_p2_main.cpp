@@ -10,7 +10,7 @@
 // The grid is P x Q with rank = P*qc + pr (528): HPL.dat's P and Q (lines 11
 // and 12) when they multiply to the rank count with P <= 2, otherwise P = 2
 // for an even rank count (the reference's fixed P = 2); one rank runs 1 x 1.
-// CHPL_P2_DRY_RUN=1 prints the configuration and exits before any GPU or
+// CHPL_DRY_RUN=1 prints the configuration and exits before any GPU or
 // network work.
 //
 // There is no MPI: rank, rank count and local rank come from the launcher's
@@ -194,7 +194,7 @@ int main(int argc, char** argv)
         if (rank == 0) std::fprintf(stderr, "[chpl_p2] the grid runs the emulated update only (CHPL2D_G8=1)\n");
         return 1;
     }
-    static const char* kDry[] = {"CHPL_P2_DRY_RUN", nullptr};
+    static const char* kDry[] = {"CHPL_DRY_RUN", nullptr};
     if (env_int(kDry, 0)) {
         if (rank == 0)
             std::printf("[chpl_p2] grid %dx%d N=%" PRId64 " NB=%" PRId64 " threshold=%g moduli=%d ranks=%d\n", P, Q,

@@ -3,6 +3,10 @@
 // Same command line, environment and report as the reference executable
 // (src/chpl_single.cu:950-965):
 //   chpl_single N                   one HPL solve of order N
+//   chpl_single HPL.dat             the same, N / NB / threshold from HPL.dat
+//                                   lines 6 / 8 / 13 (the translation the
+//                                   reference's launcher does for one GPU,
+//                                   scripts/mpirun_chpl:66-77)
 //   chpl_single --selftest          small FP64 and emulated solves
 //   chpl_single --gemmtest m k n    emulated update vs cuBLAS DGEMM
 // Environment (src/chpl_single.cu:842-869, same names and defaults):
@@ -10,7 +14,8 @@
 //   HPLS_G8_MODULI (14) HPLS_G8_FAST (0) HPLS_G8_CHUNK (16384)
 // HPLS_BACKEND=ozaki (the Ozaki-I engine) is not part of this build.
 // Exit status: 0 = passed, 1 = failed or bad arguments, 4 = the memory plan
-// does not fit the device (src/chpl_single.cu:389-394).
+// does not fit the device (src/chpl_single.cu:389-394).  CHPL_DRY_RUN=1
+// prints the configuration and exits before any GPU work.
 #include <cuda_runtime.h>
 #include <cublas_v2.h>
 
@@ -20,6 +25,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "chpl.h"
@@ -90,6 +96,31 @@ void report(const chpl_hpl_config& c, const chpl_hpl_result& r)
                 r.gemm_kernel_s > 0 ? r.gemm_int8_ops / r.gemm_kernel_s / 1e12 : 0.0);
     std::printf("==========================================================\n");
     std::fflush(stdout);
+}
+
+// N, NB, threshold from lines 6, 8 and 13 of an HPL.dat; false when the file
+// cannot be read or is shorter than 13 lines
+bool read_dat(const char* path, int64_t* N, int64_t* NB, double* thresh)
+{
+    FILE* f = std::fopen(path, "r");
+    if (!f) return false;
+    std::vector<std::string> L;
+    char ln[4096];
+    while (std::fgets(ln, sizeof(ln), f)) L.push_back(ln);
+    std::fclose(f);
+    if (L.size() < 13) return false;
+    *N = std::atoll(L[5].c_str());
+    *NB = std::atoll(L[7].c_str());
+    *thresh = std::atof(L[12].c_str());
+    return true;
+}
+
+bool is_integer(const char* s)
+{
+    if (!*s) return false;
+    for (; *s; ++s)
+        if (*s < '0' || *s > '9') return false;
+    return true;
 }
 
 int run_case(const chpl_hpl_config& c)
@@ -196,6 +227,28 @@ int main(int argc, char** argv)
         return 1;
     }
     chpl_hpl_config c;
-    if (!cfg_from_env(std::atoll(argv[1]), &c)) return 1;
+    if (is_integer(argv[1])) {
+        if (!cfg_from_env(std::atoll(argv[1]), &c)) return 1;
+    } else {
+        int64_t N = 0, NB = 0;
+        double thresh = 16.0;
+        if (!read_dat(argv[1], &N, &NB, &thresh)) {
+            std::fprintf(stderr, "[chpl_single] cannot read N/NB/threshold from '%s' (13-line HPL.dat)\n", argv[1]);
+            return 1;
+        }
+        if (!cfg_from_env(N, &c)) return 1;
+        c.NB = NB;
+        c.threshold = thresh;
+        if (c.NB <= 0 || c.NB > c.N) {
+            std::fprintf(stderr, "[chpl_single] bad N/NB/AGG\n");
+            return 1;
+        }
+    }
+    if (const char* d = std::getenv("CHPL_DRY_RUN"); d && std::atoi(d)) {
+        std::printf("[chpl_single] N=%" PRId64 " NB=%" PRId64 " AGG=%d backend=%s moduli=%d fast=%d chunk=%" PRId64
+                    " threshold=%g\n",
+                    c.N, c.NB, c.agg, c.emulate ? "gemmul8" : "native", c.moduli, c.fast, c.chunk, c.threshold);
+        return 0;
+    }
     return run_case(c);
 }

@@ -51,6 +51,24 @@ def test_p2_rejects_odd_rank_count():
     assert r.returncode == 1 and "even number of ranks" in r.stderr
 
 
+def test_single_reads_hpl_dat(tmp_path):
+    """chpl_single HPL.dat: N, NB and threshold from lines 6, 8 and 13; the
+    reference's chpl_single takes only N (its launcher translates the file)."""
+    sys.path.insert(0, ROOT)
+    from chpl_b200 import hpl
+    p = tmp_path / "HPL.dat"
+    hpl.write_hpl_dat(str(p), 139264, 1024, 1, 1, 12.5)
+    r = _run([SINGLE, str(p)], env={"CHPL_DRY_RUN": "1", "HPLS_BACKEND": "gemmul8", "HPLS_NB": "2048"})
+    assert r.returncode == 0, r.stderr
+    assert "N=139264 NB=1024 AGG=6 backend=gemmul8" in r.stdout and "threshold=12.5" in r.stdout
+    r = _run([SINGLE, "65536"], env={"CHPL_DRY_RUN": "1"})
+    assert r.returncode == 0 and "N=65536 NB=2048 AGG=6 backend=native moduli=14" in r.stdout
+    short = tmp_path / "short.dat"
+    short.write_text("x\n")
+    r = _run([SINGLE, str(short)])
+    assert r.returncode == 1 and "cannot read N/NB/threshold" in r.stderr
+
+
 def _dat(path, N, NB):
     sys.path.insert(0, ROOT)
     from chpl_b200 import hpl

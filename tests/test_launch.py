@@ -1,7 +1,7 @@
 """CPU tests of the launcher (python -m chpl_b200.launch), the MPI-free
 counterpart of the reference's scripts/mpirun_chpl, and of chpl_p2's grid
 choice.  Nothing here touches a GPU: dry runs, and chpl_p2 with
-CHPL_P2_DRY_RUN=1, which exits before any device or network work."""
+CHPL_DRY_RUN=1, which exits before any device or network work."""
 import os
 import subprocess
 import sys
@@ -17,7 +17,7 @@ P2 = os.path.join(ROOT, "chpl_b200", "bin", "chpl_p2")
 def _run(args, env=None):
     e = dict(os.environ)
     for k in list(e):
-        if k.startswith(("HPLS_", "CHPL2D_", "CHPL_P2_")):
+        if k.startswith(("HPLS_", "CHPL2D_", "CHPL_DRY")):
             del e[k]
     e.update(env or {})
     return subprocess.run([sys.executable, "-m", "chpl_b200.launch"] + args, capture_output=True, text=True,
@@ -99,7 +99,7 @@ def test_dry_run_cli():
 def test_chpl_p2_takes_the_grid_from_hpl_dat(tmp_path):
     dat = tmp_path / "HPL.dat"
     hpl.write_hpl_dat(str(dat), 196608, 4096, 1, 2)
-    base = {"CHPL_P2_DRY_RUN": "1", "RANK": "0"}
+    base = {"CHPL_DRY_RUN": "1", "RANK": "0"}
     out = subprocess.run([P2, str(dat)], env=dict(os.environ, WORLD_SIZE="2", **base), capture_output=True,
                          text=True, timeout=60)
     assert out.returncode == 0 and "grid 1x2 N=196608 NB=4096" in out.stdout
@@ -113,6 +113,6 @@ def test_launcher_starts_ranks_through_torchrun():
     """The whole chain on CPU: launcher -> torchrun (2 processes) -> chpl_p2,
     which reads its rank from torchrun's environment and the grid from the
     launcher's HPL.dat, then stops before any GPU work (dry run)."""
-    r = _run(["-P", "1", "-Q", "2", "-N", "65536"], env={"CHPL_P2_DRY_RUN": "1"})
+    r = _run(["-P", "1", "-Q", "2", "-N", "65536"], env={"CHPL_DRY_RUN": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert "[chpl_p2] grid 1x2 N=65536 NB=4096 threshold=16 moduli=11 ranks=2" in r.stdout

@@ -190,6 +190,7 @@ int main(int argc, char** argv)
     cfg.moduli = env_int(kMod, 11);
     cfg.fast = env_int(kFast, 1);
     cfg.chunk = env_int(kNT, 0);
+    cfg.verbose = 1;  // rank 0's memory plan line
     if (!cfg.emulate && size > 1) {
         if (rank == 0) std::fprintf(stderr, "[chpl_p2] the grid runs the emulated update only (CHPL2D_G8=1)\n");
         return 1;
@@ -232,6 +233,9 @@ int main(int argc, char** argv)
     }
     cudaSetDevice(local % ndev);
 
+    if (rank == 0 && cfg.emulate)   // the backend banner of src/chpl_p2.cu:764-767
+        std::printf("[chpl_p2] G8 backend on: moduli=%d fast=%d nt=%lld (grid %dx%d)\n", cfg.moduli, cfg.fast,
+                    (long long)cfg.chunk, P, Q);
     chpl_hpl_result res;
     const time_t ts0 = std::time(nullptr);
     if (size == 1) {

@@ -53,6 +53,7 @@ bool cfg_from_env(int64_t N, chpl_hpl_config* c)
     c->fast = (int)env_i64("HPLS_G8_FAST", 0);
     c->chunk = env_i64("HPLS_G8_CHUNK", 16384);
     c->seed = (uint64_t)env_i64("HPLS_SEED", 42);
+    c->verbose = 1;  // the MEM PLAN line, as src/chpl_single.cu:379-388 prints it
     c->emulate = 0;
     const char* b = std::getenv("HPLS_BACKEND");
     if (b && std::strcmp(b, "gemmul8") == 0) {

@@ -102,3 +102,37 @@ def test_host_entry_points_reject_bad_arguments_without_gpu():
     assert L.chpl_host_free(None) == _lib.CHPL_OK
     res = ctypes.c_double()
     assert L.chpl_residual_matrix(None, 10, None, 10, None, ctypes.byref(res)) == _lib.CHPL_ERR_INVALID
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/chpl.h compiles as C99 (no C++ in the ABI) and a C program links
+    against libchpl.so and calls its host-only entry points."""
+    src = tmp_path / "abi.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "chpl.h"
+int main(void) {
+    chpl_hpl_config c;
+    chpl_hpl_result r;
+    size_t tot = 0, wa = 0, wb = 0;
+    int a = 0, b = 0;
+    chpl_hpl_default_config(&c);
+    if (c.N != 16384 || c.NB != 1024 || c.moduli != 11) return 2;
+    if (chpl_oz2_worksize(4096, 4096, 4096, 11, 1, 0, &tot, &wa, &wb) != CHPL_OK || tot < wa + wb) return 3;
+    if (chpl_oz2_shift_bits(11, 4096, &a, &b) != CHPL_OK || a != 43 || b != 43) return 4;
+    c.N = -1;
+    if (chpl_hpl_run(&c, &r, NULL) != CHPL_ERR_INVALID) return 5;
+    if (strstr(chpl_version(), "sm_100a") == NULL) return 6;
+    printf("ok %s\n", chpl_version());
+    return 0;
+}
+''')
+    exe = tmp_path / "abi"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    cc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                         "-o", str(exe), "-L", libdir, "-lchpl", f"-Wl,-rpath,{libdir}"],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.startswith("ok"), (run.returncode, run.stdout, run.stderr)

@@ -3,6 +3,7 @@
     python -m chpl_b200.cases gemm --m 32768 --n 32768 --k 4096 --moduli 11 [--reps 3]
     python -m chpl_b200.cases hpl --N 65536 --NB 1024 [--no-lookahead]
     python -m chpl_b200.cases laswp --rows 139264 --cols 65536 --swaps 1024
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m chpl_b200.cases grid --N 131072 --NB 2048 --moduli 11 12
 
 Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (BASELINE
 config 2) generated on the device.
@@ -116,6 +117,37 @@ def laswp_case(rows: int, cols: int, swaps: int, reps: int) -> dict:
             "algorithmic_gb": gb, "gbs": gb / best}
 
 
+def grid_case(N: int, NB: int, moduli: list[int], grid_shape: str) -> list[dict]:
+    """BASELINE config 5 on the job's grid (run under torchrun, one process per
+    GPU): one solve per moduli count, with the per-phase device times (max over
+    ranks), the time outside the int8 GEMM kernel (max / min over ranks) and
+    the residual.  Rank 0 prints one JSON line per solve."""
+    from . import grid
+    dist = grid.init_from_env()
+    world = dist.get_world_size()
+    P, Q = grid.grid_shape(world)
+    if grid_shape:
+        P, Q = (int(v) for v in grid_shape.lower().split("x"))
+    g = grid.Grid(P, Q)
+    out = []
+    for L in moduli:
+        r = g.run(hpl.Config(N=N, NB=NB, P=P, Q=Q, moduli=L))
+        outside = r.time_s - r.gemm_kernel_s
+        row = {"case": "grid", "N": N, "NB": NB, "grid": f"{P}x{Q}", "moduli": L,
+               "tflops": hpl.flops(N) / grid.max_over_ranks(r.time_s) / 1e12, "resid": r.resid,
+               "passed": r.passed, "schedule": "lookahead" if r.schedule else "serial",
+               "phases_max_over_ranks": {p: grid.max_over_ranks(v) for p, v in r.phases.items()},
+               "gemm_kernel_s_max_over_ranks": grid.max_over_ranks(r.gemm_kernel_s),
+               "outside_gemm_s": {"max": grid.max_over_ranks(outside), "min": -grid.max_over_ranks(-outside)}}
+        out.append(row)
+        if dist.get_rank() == 0:
+            print(json.dumps(row), flush=True)
+    g.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -136,6 +168,11 @@ def main() -> None:
     lw.add_argument("--cols", type=int, default=65536)
     lw.add_argument("--swaps", type=int, default=1024)
     lw.add_argument("--reps", type=int, default=5)
+    gr = sub.add_parser("grid")
+    gr.add_argument("--N", type=int, default=131072)
+    gr.add_argument("--NB", type=int, default=2048)
+    gr.add_argument("--moduli", type=int, nargs="+", default=[11, 12])
+    gr.add_argument("--grid", default="", help="PxQ (default: 1x1, 1x2, 2x2, 2x4 by rank count)")
     h = sub.add_parser("hpl")
     h.add_argument("--N", type=int, default=16384)
     h.add_argument("--NB", type=int, default=1024)
@@ -148,6 +185,9 @@ def main() -> None:
     h.add_argument("--panel-mode", type=int, default=0)
     h.add_argument("--lookahead", action="store_true")
     a = ap.parse_args()
+    if a.what == "grid":
+        grid_case(a.N, a.NB, a.moduli, a.grid)
+        return
     torch.cuda.set_device(0)
     if a.what == "gemm":
         print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled, a.sustain)), flush=True)

@@ -136,3 +136,18 @@ int main(void) {
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.startswith("ok"), (run.returncode, run.stdout, run.stderr)
+
+
+def test_host_buffer_api_fails_loudly_without_a_gpu():
+    """No silent host fallback: without a device the pinned allocation and the
+    host-buffer solve raise ChplError (CUDA error), never compute on the CPU."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    import numpy as np
+    from chpl_b200 import hpl
+    with pytest.raises(_lib.ChplError):
+        hpl.HostSystem(64)
+    Ab = np.zeros((65, 64))
+    with pytest.raises(_lib.ChplError):
+        hpl.run_host(hpl.Config(N=64, NB=16), Ab)

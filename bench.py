@@ -384,6 +384,9 @@ def run_single(a) -> None:
         "resid": max(r.resid for r in res), "passed": all(r.passed for r in res),
         "phases_s": phases,
         "outside_gemm_s_per_step": outside,
+        # the whole solve against the update's roofline: the int8 rate divided by the moduli count
+        "hpl_roofline": {"int8_tops": peak_i8, "moduli": a.moduli, "fp64eq_tflops": peak_i8 / a.moduli,
+                         "frac": value / (peak_i8 / a.moduli)},
         "roofline": roof,
         "e2e": None,
         "gpu_launches": sum(r.n_launches for r in res),

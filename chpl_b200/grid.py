@@ -163,6 +163,10 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
             "phases_s_max_over_ranks": phases,
             "outside_gemm_s_per_step": {"max_over_ranks": outside_max, "min_over_ranks": outside_min,
                                         "note": "solve time minus the rank's own int8 GEMM kernel time"},
+            "hpl_roofline": ({"int8_tops_per_gpu": peak, "moduli": a.moduli,
+                              "fp64eq_tflops": world * peak / a.moduli,
+                              "frac": (a.steps * flops(N) / solve / 1e12) / (world * peak / a.moduli)}
+                             if peak else None),
             "roofline": {"bound": "tensor", "achieved": ops / gk / 1e12 if gk else None, "peak": peak,
                          "unit": "TOPS (int8)",
                          "frac": (ops / gk / 1e12 / peak) if (gk and peak) else None,

@@ -6,7 +6,7 @@
 One step = one HPL solve (factor + back substitution) of the generated system,
 with the matrix generated in HBM before the step's timed region (HPL excludes
 generation, src/chpl_single.cu:756-757, src/chpl_p2.cu:965-966).  Workload at
-N=1: BASELINE config 3 (N=139264, NB=1024, 1x1 grid, 11 moduli, ~155 GB).
+N=1: the single-GPU weak-scale solve (N=139264, NB=1024, 1x1 grid, 11 moduli, ~155 GB).
 Multi-GPU runs are weak-scaled to ~155 GB per GPU on the grids 1x2, 2x2, 2x4
 (config 4 at 8 GPUs: N=393216, NB=4096, P2Q4).
 

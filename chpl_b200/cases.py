@@ -5,8 +5,8 @@
     python -m chpl_b200.cases laswp --rows 139264 --cols 65536 --swaps 1024
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m chpl_b200.cases grid --N 131072 --NB 2048 --moduli 11 12
 
-Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (BASELINE
-config 2) generated on the device.
+Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (the
+standalone update's distribution), generated on the device.
 """
 from __future__ import annotations
 
@@ -118,7 +118,7 @@ def laswp_case(rows: int, cols: int, swaps: int, reps: int) -> dict:
 
 
 def grid_case(N: int, NB: int, moduli: list[int], grid_shape: str) -> list[dict]:
-    """BASELINE config 5 on the job's grid (run under torchrun, one process per
+    """The scaling-sweep case (N = 131072, NB = 2048 by default) on the job's grid (run under torchrun, one process per
     GPU): one solve per moduli count, with the per-phase device times (max over
     ranks), the time outside the int8 GEMM kernel (max / min over ranks) and
     the residual.  Rank 0 prints one JSON line per solve."""

@@ -945,14 +945,15 @@ extern "C" int chpl_oz2_gemm(void* stream, int opA, int opB, size_t m, size_t n,
         set_error("op must be CHPL_OP_N or CHPL_OP_T");
         return CHPL_ERR_INVALID;
     }
+    // arguments are validated before any early return, so a bad call never reports success
+    CHPL_TRY(check_common(num_moduli, k));
+    if (m > 0x7fffffffull || n > 0x7fffffffull) { set_error("m, n must fit in int32"); return CHPL_ERR_UNSUPPORTED; }
     if (m == 0 || n == 0) return CHPL_OK;
     if (ldc < m || lda < (opA == CHPL_OP_N ? m : k) || ldb < (opB == CHPL_OP_N ? k : n)) {
         set_error("leading dimension too small");
         return CHPL_ERR_INVALID;
     }
     if (k == 0 || *alpha == 0.0) return scale(st, C, ldc, m, n, *beta);
-    CHPL_TRY(check_common(num_moduli, k));
-    if (m > 0x7fffffffull || n > 0x7fffffffull) { set_error("m, n must fit in int32"); return CHPL_ERR_UNSUPPORTED; }
     if (!work) { set_error("work is NULL"); return CHPL_ERR_WORKSPACE; }
     const Moduli* M = moduli((int)num_moduli);
     const Layout y = layout(m, n, k, (int)num_moduli, workA != nullptr, workB != nullptr);

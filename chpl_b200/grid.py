@@ -19,7 +19,7 @@ from . import _lib, hpl
 
 
 def grid_shape(world: int) -> tuple[int, int]:
-    """BASELINE's grids: 1x1, 1x2, 2x2, 2x4 (P <= 2)."""
+    """Grid of a job with `world` GPUs: 1x1, 1x2, 2x2, 2x4 (P <= 2), else 1 x world."""
     return {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}.get(world, (1, world))
 
 

@@ -157,7 +157,8 @@ PHASES = ["panel", "laswp", "trsm", "oz2_split", "oz2_gemm", "update_fp64", "bac
 
 
 def flops(N: int) -> float:
-    """BASELINE's operation count 2/3 N^3 + 2 N^2 (the reference prints 3/2 N^2)."""
+    """Operation count of the benchmark metric, 2/3 N^3 + 2 N^2 (the reference prints 3/2 N^2,
+    src/chpl_p2.cu:1883)."""
     return (2.0 / 3.0) * N ** 3 + 2.0 * N ** 2
 
 

@@ -128,11 +128,15 @@ int chpl_oz2_products(void *stream, size_t m, size_t n, size_t k, unsigned num_m
  * whose scratch exceeds 64 MiB are rejected with CHPL_ERR_WORKSPACE (the
  * scratch is about L*(m_pad + n_pad)*k_pad bytes plus 2 MiB per modulus, with
  * m_pad, k_pad rounded up to 128 and n_pad to 256; e.g. m = n = k = 1024 at 12
- * moduli fits).  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  All calls on a device share the array and
- * it keeps the last call's contents, so calls that overlap on the GPU (other
- * streams, other host threads) race: serialize them.  Nothing is allocated.
+ * moduli fits).  The first call on each device (and again after a
+ * cudaDeviceReset, which gives the device a new context) looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  All calls on a device share the array
+ * and it keeps the last call's contents, so calls that overlap on the GPU
+ * (other streams, other host threads) race: serialize them.  Nothing is
+ * allocated.  As for chpl_oz2_gemm, a device-side wait that runs out of time
+ * leaves C undefined while the call itself has returned CHPL_OK: check
+ * chpl_device_status after synchronizing.
  */
 int chpl_oz2_gemm_noalloc(void *stream, int opA, int opB, size_t m, size_t n, size_t k, const double *alpha,
                           const double *A, size_t lda, const double *B, size_t ldb, const double *beta,

@@ -66,6 +66,23 @@ def test_shift_bits_agree_with_oracle():
         assert (a.value, b.value) == oracle.oz2_shift_bits(nm, 1000)
 
 
+def test_gemm_entry_points_validate_before_early_return():
+    """A bad moduli count or k is an error even when there is nothing to
+    compute (m, n or k zero); these checks run before any CUDA call."""
+    L = _lib.load()
+    a, b = ctypes.c_double(1.0), ctypes.c_double(1.0)
+    for m, n, k in ((4, 4, 0), (0, 4, 4), (4, 0, 4)):
+        rc = L.chpl_oz2_gemm(None, 0, 0, m, n, k, ctypes.byref(a), None, 4, None, 4, ctypes.byref(b), None, 4, 1, 1,
+                             None, None, None, 0, 0, 0, 0, None)
+        assert rc == _lib.CHPL_ERR_INVALID, (m, n, k)
+        rc = L.chpl_oz2_gemm_noalloc(None, 0, 0, m, n, k, ctypes.byref(a), None, 4, None, 4, ctypes.byref(b), None, 4,
+                                     17)
+        assert rc == _lib.CHPL_ERR_INVALID, (m, n, k)
+    rc = L.chpl_oz2_gemm(None, 0, 0, 4, 4, 131072, ctypes.byref(a), None, 4, None, 131072, ctypes.byref(b), None, 4, 11,
+                         1, None, None, None, 0, 0, 0, 0, None)
+    assert rc == _lib.CHPL_ERR_UNSUPPORTED
+
+
 def test_default_config():
     L = _lib.load()
     c = _lib.HplConfig()

@@ -1,4 +1,4 @@
-"""The standalone trailing update at its full size on a B200 (BASELINE config 2):
+"""The standalone trailing update at its full size on a B200:
 C(m x n) -= A(m x k) B(k x n), m = n = 32768, k = 4096, FP64 column-major,
 entries uniform in [-0.5, 0.5) from the reference's generator (chpl_elem of
 src/chpl_p2.cu:66-73 over each matrix's own index space; seeds 42, 43, 44 for

@@ -149,7 +149,7 @@ def test_hpl_emulated_passes(cuda, L):
 
 
 def test_hpl_config1_passes_at_11_moduli(cuda):
-    """BASELINE config 1 (N = 16384, NB = 1024, 11 moduli) with the library's
+    """The chpl_p2 fallback size (N = 16384, NB = 1024, 11 moduli) with the library's
     default aggregation passes the HPL check with margin (the aggregated
     k = 4096 form gave 23.7 here, a failure)."""
     res = hpl.run(hpl.Config(N=16384, NB=1024, moduli=11), want_x=False)

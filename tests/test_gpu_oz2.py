@@ -3,7 +3,7 @@
 Bit-exact: shifts, int8 residues, per-modulus int32 products, and the full
 emulated GEMM against the oracle's fixed-point mirror (same FP64 operations).
 Within tolerance: against exact CRT and FP64 DGEMM (rigorous error bound, and
-max|dC| / (||A||_oo ||B||_oo) <= 1e-15 at 11 moduli as BASELINE config 2 asks).
+max|dC| / (||A||_oo ||B||_oo) <= 1e-15 at 11 moduli, the standalone update's tolerance).
 """
 import os
 

@@ -15,6 +15,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from chpl_b200 import _lib, oz2
 from gpu_util import empty_bytes, from_dev, to_dev
 
@@ -58,6 +59,45 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda):
         got = _noalloc(m, n, k, L, A, B, C, opA=opA, opB=opB)
         ref = _with_work(m, n, k, L, A, B, C, opA=opA, opB=opB)
         assert np.array_equal(got, ref), (m, n, k, L)
+
+
+def test_noalloc_persistent_tiles_match(cuda):
+    """More output tiles (16 x 8 of 128 x 256) than the 64 CTAs the fixed
+    scratch allows: each CTA reuses its CRT scratch slice for several tiles."""
+    rng = np.random.default_rng(7)
+    m = n = 2048
+    k, L = 256, 12
+    A = rng.uniform(-0.5, 0.5, (m, k))
+    B = rng.uniform(-0.5, 0.5, (k, n))
+    C = rng.uniform(-0.5, 0.5, (m, n))
+    for _ in range(2):
+        got = _noalloc(m, n, k, L, A, B, C)
+        ref = _with_work(m, n, k, L, A, B, C)
+        assert np.array_equal(got, ref)
+
+
+def test_noalloc_at_documented_limit_matches_oracle(cuda):
+    """m = n = k = 1024 at 12 moduli, the size the header names as fitting,
+    checked bit for bit against the CPU oracle's emulated GEMM."""
+    rng = np.random.default_rng(11)
+    m = n = k = 1024
+    L = 12
+    A = rng.uniform(-0.5, 0.5, (m, k))
+    B = rng.uniform(-0.5, 0.5, (k, n))
+    C = rng.uniform(-0.5, 0.5, (m, n))
+    got = _noalloc(m, n, k, L, A, B, C)
+    ref = oracle.oz2_gemm(A, B, C, L, mode=1)
+    assert np.array_equal(got, ref)
+
+
+def test_noalloc_validates_before_early_return(cuda):
+    """A bad moduli count is an error even when k == 0 (nothing to multiply)."""
+    lib = _lib.load()
+    a, b = ctypes.c_double(1.0), ctypes.c_double(1.0)
+    d = torch.zeros(16, dtype=torch.float64, device="cuda")
+    rc = lib.chpl_oz2_gemm_noalloc(0, 0, 0, 4, 4, 0, ctypes.byref(a), d.data_ptr(), 4, d.data_ptr(), 1,
+                                   ctypes.byref(b), d.data_ptr(), 4, 1)
+    assert rc == _lib.CHPL_ERR_INVALID
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda):

@@ -24,6 +24,9 @@ CHPL_ERR_NO_DEVICE = -8
 CHPL_OP_N = 0
 CHPL_OP_T = 1
 
+CHPL_GEN_CHPL = 0
+CHPL_GEN_PHILOX = 1
+
 _i64 = ctypes.c_int64
 _u64 = ctypes.c_uint64
 _sz = ctypes.c_size_t
@@ -37,7 +40,7 @@ _dp = ctypes.POINTER(ctypes.c_double)
 class HplConfig(ctypes.Structure):
     _fields_ = [("N", _i64), ("NB", _i64), ("P", _int), ("Q", _int), ("moduli", _int), ("emulate", _int),
                 ("fast", _int), ("chunk", _i64), ("lookahead", _int), ("agg", _int), ("reserve_sms", _int), ("trsm_mode", _int), ("panel_mode", _int),
-                ("seed", _u64), ("threshold", _dbl), ("verbose", _int)]
+                ("seed", _u64), ("threshold", _dbl), ("verbose", _int), ("generator", _int)]
 
 
 class HplResult(ctypes.Structure):
@@ -66,6 +69,7 @@ SIGNATURES = {
     "chpl_oz2_products": (_int, [_vp, _sz, _sz, _sz, _uint, _vp, _sz, _vp, _sz, _sz, _vp, _sz]),
     "chpl_oz2_shift_bits": (_int, [_uint, _sz, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
     "chpl_matgen": (_int, [_vp, _vp, _sz, _sz, _sz, _i64, _i64, _i64, _u64]),
+    "chpl_matgen_philox": (_int, [_vp, _vp, _sz, _sz, _sz, _i64, _i64, _i64, _u64]),
     "chpl_matgen_cyclic": (_int, [_vp, _vp, _sz, _i64, _i64, _int, _int, _int, _int, _u64]),
     "chpl_matgen_host": (_int, [_i64, _u64, _vp, _sz]),
     "chpl_laswp_work_bytes": (_sz, [_i64, _i64]),

@@ -12,6 +12,9 @@
 // Environment (src/chpl_single.cu:842-869, same names and defaults):
 //   HPLS_NB (2048) HPLS_AGG (6) HPLS_BACKEND (native | gemmul8) HPLS_SEED (42)
 //   HPLS_G8_MODULI (14) HPLS_G8_FAST (0) HPLS_G8_CHUNK (16384)
+// The matrix is the reference chpl_single's: cuRAND Philox4_32_10, one
+// subsequence per element (src/chpl_single.cu:73-80).  HPLS_GEN=chpl (this
+// build's switch) selects chpl_p2's SplitMix64 matrix instead.
 // HPLS_BACKEND=ozaki (the Ozaki-I engine) is not part of this build.
 // Exit status: 0 = passed, 1 = failed or bad arguments, 4 = the memory plan
 // does not fit the device (src/chpl_single.cu:389-394).  CHPL_DRY_RUN=1
@@ -55,6 +58,16 @@ bool cfg_from_env(int64_t N, chpl_hpl_config* c)
     c->seed = (uint64_t)env_i64("HPLS_SEED", 42);
     c->verbose = 1;  // the MEM PLAN line, as src/chpl_single.cu:379-388 prints it
     c->emulate = 0;
+    c->generator = CHPL_GEN_PHILOX;
+    const char* gen = std::getenv("HPLS_GEN");
+    if (gen && *gen) {
+        if (std::strcmp(gen, "chpl") == 0) {
+            c->generator = CHPL_GEN_CHPL;
+        } else if (std::strcmp(gen, "philox") != 0) {
+            std::fprintf(stderr, "[chpl_single] unknown HPLS_GEN '%s' (philox | chpl)\n", gen);
+            return false;
+        }
+    }
     const char* b = std::getenv("HPLS_BACKEND");
     if (b && std::strcmp(b, "gemmul8") == 0) {
         c->emulate = 1;
@@ -200,6 +213,7 @@ int selftest()
     c1.agg = 4;
     c1.emulate = 0;
     c1.seed = 42;
+    c1.generator = CHPL_GEN_PHILOX;   // the reference selftest's matrix (src/chpl_single.cu:750)
     chpl_hpl_config c2 = c1;
     c2.emulate = 1;
     c2.moduli = 14;
@@ -224,7 +238,7 @@ int main(int argc, char** argv)
     if (argc != 2) {
         std::fprintf(stderr, "usage: chpl_single N | chpl_single --selftest | chpl_single --gemmtest m k n\n"
                              "env: HPLS_NB HPLS_AGG HPLS_BACKEND(native|gemmul8) HPLS_SEED HPLS_G8_MODULI "
-                             "HPLS_G8_FAST HPLS_G8_CHUNK\n");
+                             "HPLS_G8_FAST HPLS_G8_CHUNK HPLS_GEN(philox|chpl)\n");
         return 1;
     }
     chpl_hpl_config c;

@@ -1,4 +1,6 @@
 // HPL building blocks on B200: matrix generation, row interchanges, residual.
+#include <curand_kernel.h>
+
 #include <algorithm>
 #include <cstdio>
 
@@ -22,8 +24,27 @@ __device__ __forceinline__ double hpl_elem(uint64_t seed, uint64_t idx)
     return (double)(z >> 11) * (1.0 / 9007199254740992.0) - 0.5;
 }
 
+// generator of chpl_single (src/chpl_single.cu:73-80): cuRAND's
+// Philox4_32_10 with one subsequence per element (subsequence = the element's
+// index, offset 0), first uniform double in (0, 1] minus 0.5.  Computed by
+// cuRAND's own device API, so the matrix is the reference chpl_single's.
+__device__ __forceinline__ double philox_elem(uint64_t seed, uint64_t idx)
+{
+    curandStatePhilox4_32_10_t s;
+    curand_init((unsigned long long)seed, (unsigned long long)idx, 0ull, &s);
+    return curand_uniform_double(&s) - 0.5;
+}
+
+template <int G>
+__device__ __forceinline__ double gen_elem(uint64_t seed, uint64_t idx)
+{
+    if constexpr (G == CHPL_GEN_PHILOX) return philox_elem(seed, idx);
+    else return hpl_elem(seed, idx);
+}
+
 // A[i + j*lda] = elem(seed, (row0+i)*ncg + col0+j); one thread per element,
 // consecutive threads walk down a column (coalesced 8-byte stores).
+template <int G>
 __global__ void matgen_kernel(double* __restrict__ A, long long lda, long long m, long long n, long long row0,
                               long long col0, long long ncg, uint64_t seed)
 {
@@ -31,7 +52,7 @@ __global__ void matgen_kernel(double* __restrict__ A, long long lda, long long m
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
          e += (long long)gridDim.x * blockDim.x) {
         const long long i = e % m, j = e / m;
-        A[i + j * lda] = hpl_elem(seed, (uint64_t)(row0 + i) * (uint64_t)ncg + (uint64_t)(col0 + j));
+        A[i + j * lda] = gen_elem<G>(seed, (uint64_t)(row0 + i) * (uint64_t)ncg + (uint64_t)(col0 + j));
     }
 }
 
@@ -61,11 +82,20 @@ static inline int grid_for(long long work, int block)
 }
 
 int matgen(cudaStream_t st, double* A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0, int64_t ncg,
-           uint64_t seed)
+           uint64_t seed, int generator)
 {
+    if (generator != CHPL_GEN_CHPL && generator != CHPL_GEN_PHILOX) {
+        set_error("unknown generator %d", generator);
+        return CHPL_ERR_INVALID;
+    }
     if (m == 0 || n == 0) return CHPL_OK;
-    matgen_kernel<<<grid_for((long long)(m * n), 256), 256, 0, st>>>(A, (long long)lda, (long long)m, (long long)n,
-                                                                      row0, col0, ncg, seed);
+    const int g = grid_for((long long)(m * n), 256);
+    if (generator == CHPL_GEN_PHILOX)
+        matgen_kernel<CHPL_GEN_PHILOX><<<g, 256, 0, st>>>(A, (long long)lda, (long long)m, (long long)n, row0, col0, ncg,
+                                                          seed);
+    else
+        matgen_kernel<CHPL_GEN_CHPL><<<g, 256, 0, st>>>(A, (long long)lda, (long long)m, (long long)n, row0, col0, ncg,
+                                                        seed);
     CHPL_CUDA(cudaGetLastError());
     return CHPL_OK;
 }
@@ -266,12 +296,13 @@ int identity(cudaStream_t st, double* X, int64_t n)
 constexpr int kResChunks = 64;
 
 // element (i, j) of the generated N x (N+1) system; column N is b
+template <int G>
 struct GenSystem {
     long long N;
     uint64_t seed;
     __device__ __forceinline__ double at(long long i, long long j) const
     {
-        return hpl_elem(seed, (uint64_t)i * (uint64_t)(N + 1) + (uint64_t)j);
+        return gen_elem<G>(seed, (uint64_t)i * (uint64_t)(N + 1) + (uint64_t)j);
     }
 };
 
@@ -368,9 +399,11 @@ static int residual_of(cudaStream_t st, int64_t N, Sys sys, const double* x, dou
     return CHPL_OK;
 }
 
-int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid)
+int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double* resid, int generator)
 {
-    return residual_of(st, N, GenSystem{(long long)N, seed}, x, resid);
+    if (generator == CHPL_GEN_PHILOX) return residual_of(st, N, GenSystem<CHPL_GEN_PHILOX>{(long long)N, seed}, x, resid);
+    if (generator != CHPL_GEN_CHPL) { set_error("unknown generator %d", generator); return CHPL_ERR_INVALID; }
+    return residual_of(st, N, GenSystem<CHPL_GEN_CHPL>{(long long)N, seed}, x, resid);
 }
 
 int residual_matrix(cudaStream_t st, int64_t N, const double* Ab, size_t ld, const double* x, double* resid)
@@ -397,6 +430,13 @@ extern "C" int chpl_matgen(void* stream, double* A, size_t lda, size_t m, size_t
 {
     if (lda < m) { set_error("lda < m"); return CHPL_ERR_INVALID; }
     return matgen((cudaStream_t)stream, A, lda, m, n, row0, col0, ncg, seed);
+}
+
+extern "C" int chpl_matgen_philox(void* stream, double* A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0,
+                                  int64_t ncg, uint64_t seed)
+{
+    if (lda < m) { set_error("lda < m"); return CHPL_ERR_INVALID; }
+    return matgen((cudaStream_t)stream, A, lda, m, n, row0, col0, ncg, seed, CHPL_GEN_PHILOX);
 }
 
 extern "C" int chpl_matgen_host(int64_t N, uint64_t seed, double* Ab, size_t ldab)

@@ -536,6 +536,10 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     if (cfg->P != 1 || cfg->Q != 1) { set_error("chpl_hpl_run drives one GPU; use the grid driver for P x Q > 1"); return CHPL_ERR_INVALID; }
     if (cfg->emulate && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
     if (Ab && (int64_t)ldab < cfg->N) { set_error("ldab < N"); return CHPL_ERR_INVALID; }
+    if (cfg->generator != CHPL_GEN_CHPL && cfg->generator != CHPL_GEN_PHILOX) {
+        set_error("generator must be CHPL_GEN_CHPL or CHPL_GEN_PHILOX");
+        return CHPL_ERR_INVALID;
+    }
     Solver s;
     int rc = s.init(*cfg);
     if (rc != CHPL_OK) { s.destroy(); return rc; }
@@ -556,7 +560,7 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
                                           (size_t)s.ncols, cudaMemcpyHostToDevice, s.s0);
         if (e != cudaSuccess) return finish(cuda_fail(e, "[A|b] host to device", __FILE__, __LINE__));
     } else {
-        rc = matgen(s.s0, s.A, (size_t)s.ld, (size_t)s.N, (size_t)s.ncols, 0, 0, s.ncols, cfg->seed);
+        rc = matgen(s.s0, s.A, (size_t)s.ld, (size_t)s.N, (size_t)s.ncols, 0, 0, s.ncols, cfg->seed, cfg->generator);
         if (rc != CHPL_OK) return finish(rc);
     }
     cudaEventRecord(g1, s.s0);
@@ -588,7 +592,7 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     // x = column N
     const double* dx = s.at(0, s.N);
     if (!Ab) {
-        rc = residual(s.s0, s.N, cfg->seed, dx, &res->resid);
+        rc = residual(s.s0, s.N, cfg->seed, dx, &res->resid, cfg->generator);
         if (rc != CHPL_OK) return finish(rc);
     } else if (verify) {
         CHPL_CUDA_OR(cudaMalloc((void**)&xs, row_bytes), finish);
@@ -645,6 +649,7 @@ extern "C" void chpl_hpl_default_config(chpl_hpl_config* cfg)
     cfg->seed = 42;
     cfg->threshold = 16.0;
     cfg->verbose = 0;
+    cfg->generator = CHPL_GEN_CHPL;
 }
 
 extern "C" int chpl_hpl_run(const chpl_hpl_config* cfg, chpl_hpl_result* res, double* x_out)

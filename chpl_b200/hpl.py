@@ -92,6 +92,7 @@ class Config:
     seed: int = 42
     threshold: float = 16.0
     verbose: bool = False
+    generator: int = _lib.CHPL_GEN_CHPL    # CHPL_GEN_PHILOX: chpl_single's cuRAND Philox matrix
 
     def to_c(self) -> _lib.HplConfig:
         c = _lib.HplConfig()
@@ -99,6 +100,7 @@ class Config:
         c.moduli, c.emulate, c.fast, c.chunk = self.moduli, int(self.emulate), int(self.fast), self.chunk
         c.lookahead, c.seed, c.threshold, c.verbose = int(self.lookahead), self.seed, self.threshold, int(self.verbose)
         c.agg, c.reserve_sms, c.trsm_mode, c.panel_mode = self.agg, self.reserve_sms, self.trsm_mode, self.panel_mode
+        c.generator = self.generator
         return c
 
 
@@ -107,15 +109,21 @@ def single_config_from_env(N: int, env=None) -> Config:
     scripts/mpirun_chpl:71-76).  HPLS_AGG groups panels into super-blocks whose
     trailing update runs with k = AGG * NB (0 = automatic: k = 4096 from
     N = 65536 up, k = NB below, where deeper emulated updates cost residual
-    margin)."""
+    margin).  The matrix is chpl_single's cuRAND Philox one
+    (src/chpl_single.cu:73-80); HPLS_GEN=chpl (this build's switch) selects
+    chpl_p2's SplitMix64 matrix instead."""
     env = os.environ if env is None else env
     backend = env.get("HPLS_BACKEND", "gemmul8")
     if backend not in ("native", "gemmul8", "ozaki"):
         raise ValueError(f"unknown HPLS_BACKEND '{backend}'")
+    gen = env.get("HPLS_GEN", "philox")
+    if gen not in ("philox", "chpl"):
+        raise ValueError(f"unknown HPLS_GEN '{gen}'")
     c = Config(N=N, NB=_env_int(env, "HPLS_NB", 1024), moduli=_env_int(env, "HPLS_G8_MODULI", 11),
                emulate=backend != "native", fast=bool(_env_int(env, "HPLS_G8_FAST", 1)),
                chunk=_env_int(env, "HPLS_G8_CHUNK", 0), seed=_env_int(env, "HPLS_SEED", 42),
-               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 0)), agg=_env_int(env, "HPLS_AGG", 0))
+               lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 0)), agg=_env_int(env, "HPLS_AGG", 0),
+               generator=_lib.CHPL_GEN_PHILOX if gen == "philox" else _lib.CHPL_GEN_CHPL)
     if c.N <= 0 or c.NB <= 0 or c.NB > c.N:
         raise ValueError("bad N/NB")
     return c

@@ -34,6 +34,10 @@ extern "C" {
 #define CHPL_OP_N 0
 #define CHPL_OP_T 1
 
+/* matrix generators (chpl_hpl_config.generator) */
+#define CHPL_GEN_CHPL 0   /* SplitMix64 hash of chpl_p2 / chpl_p4 (chpl_elem, src/chpl_p2.cu:66-73) */
+#define CHPL_GEN_PHILOX 1 /* cuRAND Philox4_32_10 of chpl_single (hs_rand, src/chpl_single.cu:73-80) */
+
 /* Human-readable description of the last error on this host thread. */
 const char *chpl_last_error_string(void);
 /* Library version string, e.g. "chpl_b200 0.1 (sm_100a)". */
@@ -156,6 +160,13 @@ int chpl_oz2_shift_bits(unsigned num_moduli, size_t k, int *alpha_bits, int *bet
  */
 int chpl_matgen(void *stream, double *A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0,
                 int64_t ncg, uint64_t seed);
+/* The same block with chpl_single's generator: element index
+ * (row0+i)*ncg + col0+j is the cuRAND Philox4_32_10 subsequence (offset 0,
+ * seed), value curand_uniform_double - 0.5, computed through cuRAND's device
+ * API.  Replaces matgen_kernel + hs_rand of src/chpl_single.cu:73-94 (called
+ * there with ncg = N + 1). */
+int chpl_matgen_philox(void *stream, double *A, size_t lda, size_t m, size_t n, int64_t row0, int64_t col0,
+                       int64_t ncg, uint64_t seed);
 /* Block-cyclic local piece of the N x (N+1) system for grid coordinate
  * (pr, qc) of a P x Q grid with block NB (src/chpl_p2.cu:615-626,951-957). */
 int chpl_matgen_cyclic(void *stream, double *A, size_t lda, int64_t N, int64_t NB, int P, int Q, int pr,
@@ -191,7 +202,7 @@ int chpl_panel_getrf_f64(void *stream, int64_t m, int64_t n, double *A, size_t l
 
 /*
  * HPL scaled residual of x (device, N) for the generated N x (N+1) system
- * (regenerated on the fly, b = column N): ||Ax-b||_oo /
+ * (CHPL_GEN_CHPL, regenerated on the fly, b = column N): ||Ax-b||_oo /
  * (eps*(||A||_oo*||x||_oo+||b||_oo)*N), eps = 2^-53.  Synchronizes.
  * Replaces the verification of src/chpl_single.cu:762-817 /
  * src/chpl_p2.cu:1886-1932.
@@ -236,6 +247,8 @@ typedef struct chpl_hpl_config {
     uint64_t seed;      /* 42 */
     double threshold;   /* HPL.dat line 13 (16.0) */
     int verbose;        /* print progress lines */
+    int generator;      /* CHPL_GEN_CHPL (default; chpl_p2's matrix) or CHPL_GEN_PHILOX (chpl_single's matrix);
+                           one-GPU runs only, the grid driver generates with CHPL_GEN_CHPL as chpl_p2 does */
 } chpl_hpl_config;
 
 typedef struct chpl_hpl_result {

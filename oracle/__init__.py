@@ -17,11 +17,15 @@ or ``__graft_entry__.build()``) restates the reference's arithmetic:
   (``src/chpl_single.cu:489-518``) and the HPL scaled residual
   (``src/chpl_single.cu:785-802``).
 
-Parity pins: SplitMix64 published known answers; exact CRT against Python
-big integers; LU against LAPACK (scipy); GEMM against numpy FP64.  GEMMul8's
-own outputs are not available (submodule absent), so kernel-level parity with
-GEMMul8 is unpinned; the reference's own end-to-end check (HPL residual < 16,
-``src/chpl_single.cu:931-948``) is the anchor.
+Parity pins: the reference's own generator (``chpl_elem``), swap resolution
+(``resolve_seq``), residual reduction and chpl_single's Philox generator
+kernel, cut verbatim out of the reference checkout and compiled into
+``oracle/_ref/`` by ``oracle/ref_build.py`` (``tests/test_oracle_ref.py``);
+SplitMix64 published known answers; exact CRT against Python big integers; LU
+against LAPACK (scipy); GEMM against numpy FP64.  GEMMul8's own outputs are not
+available (submodule absent), so kernel-level parity with GEMMul8 is unpinned;
+the reference's own end-to-end check (HPL residual < 16,
+``src/chpl_single.cu:931-948``) is the anchor there.
 """
 from __future__ import annotations
 
@@ -42,10 +46,12 @@ _ptr = ctypes.c_void_p
 
 
 def build() -> str:
-    """Compile oracle.c (gcc) into oracle/_build/liboracle.so."""
+    """Compile oracle.c (gcc) into oracle/_build/liboracle.so, and oracle/_ref/
+    from the reference's own source where the reference checkout is present."""
     src = os.path.join(_HERE, "oracle.c")
     if not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
         subprocess.check_call(["make", "-s", "-C", _HERE])
+    build_ref()
     return _SO
 
 
@@ -56,6 +62,8 @@ def lib():
         L = ctypes.CDLL(_SO)
         L.orc_splitmix64.restype = ctypes.c_uint64
         L.orc_splitmix64.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+        L.orc_hpl_residual_parts.restype = _dbl
+        L.orc_hpl_residual_parts.argtypes = [_ptr, _ptr, _ptr, _ptr, _i64]
         L.orc_elem.restype = _dbl
         L.orc_elem.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
         L.orc_matgen.argtypes = [_ptr, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint64]
@@ -219,6 +227,70 @@ def hpl_solve(N: int, NB: int, L: int = 0, seed: int = 42):
 def hpl_residual(x: np.ndarray, N: int, seed: int = 42) -> float:
     A = np.asfortranarray(hpl_system(N, seed))
     return float(lib().orc_hpl_residual(_p(A), N, N, _p(np.ascontiguousarray(x, np.float64))))
+
+
+def hpl_residual_parts(y: np.ndarray, rs: np.ndarray, b: np.ndarray, x: np.ndarray) -> float:
+    """Scaled residual from per-row data (y = A x, rs = row sums of |A|, b, x):
+    the reduction and formula of src/chpl_single.cu:790-801."""
+    N = len(y)
+    f = [np.ascontiguousarray(v, np.float64) for v in (y, rs, b, x)]
+    return float(lib().orc_hpl_residual_parts(*[_p(v) for v in f], N))
+
+
+# ---------------------------------------------------------------------------
+# oracle/_ref: fragments of the reference's own source (oracle/ref_build.py)
+# ---------------------------------------------------------------------------
+_REF = os.path.join(_HERE, "_ref")
+_ref_host = None
+
+
+def build_ref() -> bool:
+    """Build oracle/_ref/ when the reference checkout is present (False otherwise)."""
+    from . import ref_build
+    return ref_build.build()
+
+
+def ref_host():
+    """ctypes handle of oracle/_ref/libref_host.so (the reference's own
+    generator, swap resolution and residual reduction), or None if it was
+    never built (no reference checkout where the repository was built)."""
+    global _ref_host
+    if _ref_host is None:
+        so = os.path.join(_REF, "libref_host.so")
+        if not os.path.exists(so):
+            return None
+        L = ctypes.CDLL(so)
+        L.ref_chpl_elem.restype = _dbl
+        L.ref_chpl_elem.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+        L.ref_matgen.restype = None
+        L.ref_matgen.argtypes = [_ptr, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint64]
+        L.ref_resolve_seq.restype = None
+        L.ref_resolve_seq.argtypes = [_ptr, ctypes.c_longlong, ctypes.c_int, _ptr, _ptr, _ptr,
+                                      ctypes.POINTER(ctypes.c_int)]
+        L.ref_residual.restype = _dbl
+        L.ref_residual.argtypes = [_ptr, _ptr, _ptr, _ptr, _i64]
+        _ref_host = L
+    return _ref_host
+
+
+def ref_single_matgen_path() -> str | None:
+    """Path of oracle/_ref/libref_single_matgen.so (chpl_single's own Philox
+    generator kernel, sm_100a), or None if it was never built."""
+    so = os.path.join(_REF, "libref_single_matgen.so")
+    return so if os.path.exists(so) else None
+
+
+def ref_resolve_seq(piv: np.ndarray, base: int) -> tuple[np.ndarray, dict]:
+    """The reference's resolve_seq: (top, {row >= base+n: original row})."""
+    L = ref_host()
+    n = len(piv)
+    p = np.ascontiguousarray(piv, np.int64)
+    top = np.zeros(n, np.int64)
+    bp = np.zeros(max(n, 1), np.int64)
+    bs = np.zeros(max(n, 1), np.int64)
+    nb = ctypes.c_int()
+    L.ref_resolve_seq(_p(p), base, n, _p(top), _p(bp), _p(bs), ctypes.byref(nb))
+    return top, {int(bp[i]): int(bs[i]) for i in range(nb.value)}
 
 
 def hpl_residual_from(A: np.ndarray, x: np.ndarray) -> float:

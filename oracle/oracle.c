@@ -433,19 +433,37 @@ int orc_hpl_solve(double *A, int64_t lda, int64_t N, int64_t NB, int L, int64_t 
     return 0;
 }
 
-/* scaled residual of x against the regenerated system (A N x (N+1), b = col N) */
-double orc_hpl_residual(const double *A, int64_t lda, int64_t N, const double *x)
+/* The scaled residual from per-row data, the reduction and formula of
+ * src/chpl_single.cu:790-801 (also src/chpl_p2.cu:1925-1932): y = A x,
+ * rs = row sums of |A|, b, x (all N long); eps = 2^-53. */
+double orc_hpl_residual_parts(const double *y, const double *rs, const double *b, const double *x, int64_t N)
 {
     double rmax = 0.0, anorm = 0.0, xnorm = 0.0, bnorm = 0.0;
     for (int64_t i = 0; i < N; ++i) {
-        double ax = 0.0, rs = 0.0;
-        for (int64_t c = 0; c < N; ++c) { ax += A[i + c * lda] * x[c]; rs += fabs(A[i + c * lda]); }
-        const double b = A[i + N * lda];
-        if (fabs(ax - b) > rmax) rmax = fabs(ax - b);
-        if (rs > anorm) anorm = rs;
+        const double r = fabs(y[i] - b[i]);
+        if (r > rmax) rmax = r;
+        if (rs[i] > anorm) anorm = rs[i];
         if (fabs(x[i]) > xnorm) xnorm = fabs(x[i]);
-        if (fabs(b) > bnorm) bnorm = fabs(b);
+        if (fabs(b[i]) > bnorm) bnorm = fabs(b[i]);
     }
     const double eps = ldexp(1.0, -53);
     return rmax / (eps * (anorm * xnorm + bnorm) * (double)N);
+}
+
+/* scaled residual of x against the regenerated system (A N x (N+1), b = col N) */
+double orc_hpl_residual(const double *A, int64_t lda, int64_t N, const double *x)
+{
+    double *y = (double *)malloc((size_t)N * sizeof(double));
+    double *rs = (double *)malloc((size_t)N * sizeof(double));
+    if (!y || !rs) { free(y); free(rs); return NAN; }
+    for (int64_t i = 0; i < N; ++i) {
+        double ax = 0.0, s = 0.0;
+        for (int64_t c = 0; c < N; ++c) { ax += A[i + c * lda] * x[c]; s += fabs(A[i + c * lda]); }
+        y[i] = ax;
+        rs[i] = s;
+    }
+    const double r = orc_hpl_residual_parts(y, rs, A + N * lda, x, N);
+    free(y);
+    free(rs);
+    return r;
 }

@@ -76,6 +76,10 @@ SIGNATURES = {
     "chpl_laswp": (_int, [_vp, _vp, _sz, _i64, _i64, _i64, _vp, _i64, _vp]),
     "chpl_panel_getrf_work_bytes": (_sz, [_i64, _i64]),
     "chpl_panel_getrf_f64": (_int, [_vp, _i64, _i64, _vp, _sz, _vp, _vp, _vp]),
+    "chpl_dgemm": (_int, [_vp, _i64, _i64, _i64, _dbl, _vp, _sz, _vp, _sz, _dbl, _vp, _sz]),
+    "chpl_dtrsm_llnu": (_int, [_vp, _i64, _i64, _vp, _sz, _vp, _sz]),
+    "chpl_dtrsv_unn": (_int, [_vp, _i64, _vp, _sz, _vp, _vp]),
+    "chpl_dgemv": (_int, [_vp, _i64, _i64, _dbl, _vp, _sz, _vp, _dbl, _vp]),
     "chpl_residual": (_int, [_vp, _i64, _u64, _vp, _dp]),
     "chpl_residual_matrix": (_int, [_vp, _i64, _vp, _sz, _vp, _dp]),
     "chpl_hpl_default_config": (None, [ctypes.POINTER(HplConfig)]),

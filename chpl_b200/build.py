@@ -26,8 +26,8 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
                   "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
-LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu", "hpl_grid.cu",
-               "diag.cu"]
+LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "fp64.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu",
+               "hpl_grid.cu", "diag.cu"]
 def _nccl_dir() -> str:
     """NCCL bundled with torch (the same library torch.distributed loads), so
     one NCCL lives in the process; falls back to the system copy."""
@@ -45,7 +45,7 @@ NCCL_DIR = _nccl_dir()
 NCCL_INC = ["-I", os.path.join(NCCL_DIR, "include")] if NCCL_DIR else []
 NCCL_LINK = (["-L", os.path.join(NCCL_DIR, "lib"), "-l:libnccl.so.2", "-Xlinker", "-rpath," + os.path.join(NCCL_DIR, "lib")]
              if NCCL_DIR else ["-lnccl"])
-LINK = ["-cudart", "shared", "-lcublas", "-lcusolver"] + NCCL_LINK + ["-Xlinker", "-rpath," + os.path.join(CUDA, "lib64")]
+LINK = ["-cudart", "shared"] + NCCL_LINK + ["-Xlinker", "-rpath," + os.path.join(CUDA, "lib64")]
 EXES = {"chpl_single": "chpl_single_main.cpp", "chpl_p2": "chpl_p2_main.cpp"}
 
 

@@ -5,7 +5,8 @@
 // Same input and report as the reference executable (src/chpl_p2.cu:518-1953):
 // HPL.dat lines 6 (N), 8 (NB) and 13 (threshold), with N=16384, NB=1024,
 // 16.0 when the file is missing or shorter than 13 lines (570-584);
-// CHPL2D_G8 (must be 1: the emulated update), CHPL2D_G8_MODULI (11),
+// CHPL2D_G8 (1: the Ozaki-II emulated update; 0: the FP64 update, serial
+// block steps), CHPL2D_G8_MODULI (11),
 // CHPL2D_G8_FAST, CHPL2D_G8_NT (column chunk of the update) (685-691).
 // The grid is P x Q with rank = P*qc + pr (528): HPL.dat's P and Q (lines 11
 // and 12) when they multiply to the rank count with P <= 2, otherwise P = 2
@@ -191,10 +192,6 @@ int main(int argc, char** argv)
     cfg.fast = env_int(kFast, 1);
     cfg.chunk = env_int(kNT, 0);
     cfg.verbose = 1;  // rank 0's memory plan line
-    if (!cfg.emulate && size > 1) {
-        if (rank == 0) std::fprintf(stderr, "[chpl_p2] the grid runs the emulated update only (CHPL2D_G8=1)\n");
-        return 1;
-    }
     static const char* kDry[] = {"CHPL_DRY_RUN", nullptr};
     if (env_int(kDry, 0)) {
         if (rank == 0)

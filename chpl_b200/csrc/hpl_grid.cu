@@ -27,7 +27,6 @@
 // over process rows.  Communicators come from one unique id and
 // ncclCommSplit; a host watchdog aborts them (ncclCommAbort) if a step does
 // not finish within the configured timeout.
-#include <cublas_v2.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -42,6 +41,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fp64.h"
 #include "hpl.h"
 #include "oz2.h"
 
@@ -54,14 +54,6 @@ namespace chpl {
             set_error("NCCL error %d (%s) in %s at %s:%d", (int)r_, ncclGetErrorString(r_), #call, __FILE__, \
                       __LINE__);                                                                          \
             return CHPL_ERR_NCCL;                                                                         \
-        }                                                                                                 \
-    } while (0)
-#define CHPL_CUBLAS_G(call)                                                                               \
-    do {                                                                                                  \
-        cublasStatus_t s_ = (call);                                                                       \
-        if (s_ != CUBLAS_STATUS_SUCCESS) {                                                                \
-            set_error("cuBLAS error %d in %s at %s:%d", (int)s_, #call, __FILE__, __LINE__);              \
-            return CHPL_ERR_CUDA;                                                                         \
         }                                                                                                 \
     } while (0)
 
@@ -301,6 +293,7 @@ struct Emu {
     void* work = nullptr;   // B part + scratch + split temporaries
     int64_t chunk = 32768;
     int grid_cap = 0;       // > 0: persistent GEMM grid limit (SMs left to concurrent communication)
+    bool fp64 = false;      // CHPL2D_G8=0: the update runs as an FP64 DGEMM (src/chpl_p2.cu:1697-1700)
     int64_t launches = 0, gemm_n = 0;
     double ops = 0.0, flops = 0.0, kernel_s = 0.0;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
@@ -311,6 +304,12 @@ struct Emu {
             const double* B, int64_t ldb, double* C, int64_t ldc, double alpha, double beta)
     {
         if (m <= 0 || n <= 0 || k <= 0) return CHPL_OK;
+        if (fp64) {   // C must not alias B here: the FP64 U12 step goes through u12_fp64
+            CHPL_TRY(dgemm(st, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc));
+            ++launches;
+            flops += 2.0 * (double)m * (double)n * (double)k;
+            return CHPL_OK;
+        }
         for (int64_t c = 0; c < n;) {
             int64_t w = std::min(chunk, n - c);
             if (n - c - w > 0 && n - c - w < 1024) w = n - c;
@@ -349,7 +348,7 @@ struct Emu {
     // residues of A (m x k) into wa, the layout run() reads with split_a = false
     int split_only(cudaStream_t st, void* wa, int64_t m, int64_t k, const double* A, int64_t lda)
     {
-        if (m <= 0 || k <= 0) return CHPL_OK;
+        if (m <= 0 || k <= 0 || fp64) return CHPL_OK;
         const oz2::Layout y = oz2::layout((size_t)m, 256, (size_t)k, L, true, false, grid_cap);
         uint8_t* pa = static_cast<uint8_t*>(wa);
         CHPL_TRY(oz2::split(st, false, A, (size_t)lda, (size_t)m, (size_t)k, L, M->alpha,
@@ -377,7 +376,6 @@ struct GridSolver {
     chpl_hpl_config cfg{};
     int64_t N = 0, NB = 0, NBp = 0, mloc = 0, nloc = 0, lda = 0, nblk = 0;
     cudaStream_t st = nullptr;
-    cublasHandle_t hb = nullptr;
     double* A = nullptr;
     double* arena = nullptr;       // factor phase: gathered panel, pack buffer, inner residues; update phase: W, U12, W residues
     size_t arena_elems = 0;
@@ -441,8 +439,6 @@ struct GridSolver {
         int lo = 0, hi = 0;
         CHPL_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
         CHPL_CUDA(cudaStreamCreateWithPriority(&st, cudaStreamNonBlocking, hi));
-        CHPL_CUBLAS_G(cublasCreate(&hb));
-        CHPL_CUBLAS_G(cublasSetStream(hb, st));
         const unsigned L = (unsigned)cfg.moduli;
         emu.L = (int)L;
         emu.M = oz2::moduli(cfg.moduli);
@@ -465,8 +461,11 @@ struct GridSolver {
         // one arena, two phases that never overlap: factor = [gathered panel | pack | inner-update residues],
         // update = [W | U12 | residues of W]
         const size_t g_bytes = round_up(g_elems * 8, 256), wu_bytes = round_up(wu_elems * 8, 256);
-        la = g->P == 1 && g->Q > 1 && !getenv_flag("CHPL_GRID_SERIAL");
-        if (g->P == 2 && !getenv_flag("CHPL_GRID_SERIAL")) {
+        // the FP64 update (CHPL2D_G8=0) runs the serial block steps: the lookahead schedules release
+        // W's FP64 copy as soon as its int8 residues exist
+        emu.fp64 = !cfg.emulate;
+        la = cfg.emulate && g->P == 1 && g->Q > 1 && !getenv_flag("CHPL_GRID_SERIAL");
+        if (cfg.emulate && g->P == 2 && !getenv_flag("CHPL_GRID_SERIAL")) {
             // P = 2 lookahead: W slots (also the gathered panel), W residues, inner-update residues,
             // bulk and urgent U12, pack buffer; used instead of the arena
             const size_t wd = round_up(wd_elems() * 8, 256);
@@ -592,8 +591,18 @@ struct GridSolver {
         }
         panel_ev.clear();
         if (sm) cudaStreamDestroy(sm);
-        if (hb) cublasDestroy(hb);
         if (st) cudaStreamDestroy(st);
+    }
+
+    // A12 (K x n, ld lda) = inv(L11) A12 in FP64: the product goes to T (K x n,
+    // ld K) and is copied back, since a DGEMM must not write its own input
+    int u12_fp64(int64_t K, int64_t n, double* A12, double* T)
+    {
+        CHPL_TRY(dgemm(st, K, n, K, 1.0, linv, K, A12, lda, 0.0, T, K));
+        CHPL_CUDA(cudaMemcpy2DAsync(A12, (size_t)lda * 8, T, (size_t)K * 8, (size_t)K * 8, (size_t)n,
+                                    cudaMemcpyDeviceToDevice, st));
+        ++n_launch;
+        return CHPL_OK;
     }
 
     // exact partial pivoting LU of an m x K panel (ld) in place, internal
@@ -602,7 +611,6 @@ struct GridSolver {
 
     int factor_panel_p(double* Pm, int64_t ldp, int64_t m, int64_t K, int64_t* piv)
     {
-        const double one = 1.0;
         for (int64_t jp = 0; jp < K; jp += NBp) {
             const int64_t nb = std::min(NBp, K - jp);
             CHPL_TRY(panel_getrf(st, m - jp, nb, Pm + jp + jp * ldp, (size_t)ldp, piv + jp, jp, info, pwork));
@@ -612,8 +620,8 @@ struct GridSolver {
             n_launch += 4 + 2 * ((nb + 15) / 16) * 2;
             const int64_t nr = K - jp - nb;
             if (nr > 0) {
-                CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, nb,
-                                             nr, &one, Pm + jp + jp * ldp, ldp, Pm + jp + (jp + nb) * ldp, ldp));
+                CHPL_TRY(dtrsm_llnu(st, nb, nr, Pm + jp + jp * ldp, ldp, Pm + jp + (jp + nb) * ldp, ldp));
+                n_launch += dtrsm_launches(nb);
                 CHPL_TRY(emu.run(st, win, true, m - jp - nb, nr, nb, Pm + (jp + nb) + jp * ldp, ldp, Pm + jp + (jp + nb) * ldp,
                                  ldp, Pm + (jp + nb) + (jp + nb) * ldp, ldp, -1.0, 1.0));
             }
@@ -651,7 +659,6 @@ struct GridSolver {
         const int64_t ntr = nloc - tc0;
         const int64_t lrw = local_extent(J + K, NB, P, pr);        // first local row below the diagonal block
         const int64_t mW = mloc - lrw;
-        const double one = 1.0;
         auto t0 = std::chrono::steady_clock::now();
 
         // ---- 1. factor the block column on its diagonal owner ----
@@ -688,8 +695,8 @@ struct GridSolver {
         if (pr == ps) {
             if (qc == qs) {
                 CHPL_TRY(identity(st, linv, K));
-                CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K, K,
-                                             &one, A + lrb + lc * lda, lda, linv, K));
+                CHPL_TRY(dtrsm_llnu(st, K, K, A + lrb + lc * lda, lda, linv, K));
+                n_launch += dtrsm_launches(K);
                 ++n_launch;
             }
             if (g->Q > 1) CHPL_NCCL(ncclBroadcast(linv, linv, (size_t)K * K, ncclDouble, qs, g->row, st));
@@ -748,8 +755,11 @@ struct GridSolver {
         // ---- 4. U12 on the diagonal process row, down the process columns ----
         if (ntr > 0) {
             if (pr == ps) {
-                CHPL_TRY(emu.run(st, wlinv, true, K, ntr, K, linv, K, A + lrb + tc0 * lda, lda, A + lrb + tc0 * lda, lda, 1.0,
-                                 0.0));
+                if (emu.fp64)
+                    CHPL_TRY(u12_fp64(K, ntr, A + lrb + tc0 * lda, U));
+                else
+                    CHPL_TRY(emu.run(st, wlinv, true, K, ntr, K, linv, K, A + lrb + tc0 * lda, lda, A + lrb + tc0 * lda, lda,
+                                     1.0, 0.0));
                 if (P > 1)
                     CHPL_CUDA(cudaMemcpy2DAsync(U, (size_t)K * 8, A + lrb + tc0 * lda, (size_t)lda * 8, (size_t)K * 8,
                                                 (size_t)ntr, cudaMemcpyDeviceToDevice, st));
@@ -799,9 +809,8 @@ struct GridSolver {
         CHPL_TRY(factor_panel_p(A + J + lc * lda, lda, N - J, K, pv));
         CHPL_CUDA(cudaEventRecord(e1, st));
         CHPL_TRY(identity(st, lv, K));
-        const double one = 1.0;
-        CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K, K, &one,
-                                     A + J + lc * lda, lda, lv, K));
+        CHPL_TRY(dtrsm_llnu(st, K, K, A + J + lc * lda, lda, lv, K));
+        n_launch += dtrsm_launches(K);
         const int64_t mW = N - J - K;
         if (mW > 0)
             CHPL_CUDA(cudaMemcpy2DAsync(arena, (size_t)mW * 8, A + J + K + lc * lda, (size_t)lda * 8, (size_t)mW * 8,
@@ -1027,9 +1036,8 @@ struct GridSolver {
             }
             CHPL_CUDA(cudaEventRecord(evG, st));   // the W slots hold no panel any more
             CHPL_TRY(identity(st, lv, K1));
-            const double one = 1.0;
-            CHPL_CUBLAS_G(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, K1, K1,
-                                         &one, A + lrb1 + lc1 * lda, lda, lv, K1));
+            CHPL_TRY(dtrsm_llnu(st, K1, K1, A + lrb1 + lc1 * lda, lda, lv, K1));
+            n_launch += dtrsm_launches(K1);
             if (mW1 > 0)
                 CHPL_CUDA(cudaMemcpy2DAsync(Wslot, (size_t)mW1 * 8, A + lrw1 + lc1 * lda, (size_t)lda * 8, (size_t)mW1 * 8,
                                             (size_t)K1, cudaMemcpyDeviceToDevice, st));
@@ -1187,7 +1195,6 @@ struct GridSolver {
         const int64_t lcN = local_extent(N, NB, Q, qN);
         CHPL_CUDA(cudaMemsetAsync(tsum, 0, (size_t)std::max<int64_t>(mloc, 1) * 8, st));
         CHPL_CUDA(cudaMemsetAsync(x, 0, (size_t)N * 8, st));
-        const double one = 1.0;
         for (int64_t j = nblk - 1; j >= 0; --j) {
             const int64_t J = j * NB, jb = std::min(NB, N - J);
             const int pj = (int)(j % P), qj = (int)(j % Q);
@@ -1200,8 +1207,8 @@ struct GridSolver {
                 if (Q > 1) CHPL_NCCL(ncclReduce(v, v, (size_t)jb, ncclDouble, ncclSum, qj, g->row, st));
                 if (qc == qj) {
                     const int64_t lcj = local_extent(J, NB, Q, qj);
-                    CHPL_CUBLAS_G(cublasDtrsv_64(hb, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N, CUBLAS_DIAG_NON_UNIT, jb,
-                                                 A + lrj + lcj * lda, lda, v, 1));
+                    CHPL_TRY(dtrsv_unn(st, jb, A + lrj + lcj * lda, lda, v, vbuf + NB));
+                    n_launch += dtrsv_launches(jb);
                 }
             }
             if (qc == qj) {
@@ -1209,7 +1216,8 @@ struct GridSolver {
                 const int64_t lcj = local_extent(J, NB, Q, qj);
                 const int64_t rows_above = local_extent(J, NB, P, pr);
                 if (rows_above > 0)
-                    CHPL_CUBLAS_G(cublasDgemv_64(hb, CUBLAS_OP_N, rows_above, jb, &one, A + lcj * lda, lda, v, 1, &one, tsum, 1));
+                    CHPL_TRY(dgemv_n(st, rows_above, jb, 1.0, A + lcj * lda, lda, v, 1.0, tsum));
+                    ++n_launch;
                 if (pr == 0) CHPL_CUDA(cudaMemcpyAsync(x + J, v, (size_t)jb * 8, cudaMemcpyDeviceToDevice, st));
             }
         }
@@ -1266,7 +1274,6 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     if (cfg->P != g->P || cfg->Q != g->Q) { set_error("config grid %dx%d != communicator grid %dx%d", cfg->P, cfg->Q, g->P, g->Q); return CHPL_ERR_INVALID; }
     if (g->P > 2) { set_error("process grids with P > 2 are not supported (P = 1 or 2)"); return CHPL_ERR_UNSUPPORTED; }
     if (cfg->N <= 0 || cfg->NB <= 0 || cfg->NB > 16384) { set_error("bad N/NB"); return CHPL_ERR_INVALID; }
-    if (!cfg->emulate) { set_error("the grid driver runs the emulated update only (CHPL2D_G8=1)"); return CHPL_ERR_UNSUPPORTED; }
     GridSolver s;
     int rc = s.init(g, *cfg);
     auto finish = [&](int code) { s.destroy(); return code; };

@@ -17,9 +17,8 @@
 // Depth-1 lookahead (cfg.lookahead): the columns of panel k+1 are updated
 // first, on the high-priority stream sP, which then factors panel k+1 while
 // the low-priority stream s0 updates the remaining columns of step k.
-#include <cublas_v2.h>
-#include <cusolverDn.h>
-
+// Every FP64 step (triangular solves, the FP64 update, the back substitution)
+// runs on this library's kernels (fp64.cu): no cuBLAS / cuSOLVER call.
 #include <chrono>
 #include <cinttypes>
 #include <cmath>
@@ -28,27 +27,11 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fp64.h"
 #include "hpl.h"
 #include "oz2.h"
 
 namespace chpl {
-
-#define CHPL_CUBLAS(call)                                                          \
-    do {                                                                           \
-        cublasStatus_t s_ = (call);                                                \
-        if (s_ != CUBLAS_STATUS_SUCCESS) {                                         \
-            set_error("cuBLAS error %d in %s at %s:%d", (int)s_, #call, __FILE__, __LINE__); \
-            return CHPL_ERR_CUDA;                                                  \
-        }                                                                          \
-    } while (0)
-#define CHPL_CUSOLVER(call)                                                        \
-    do {                                                                           \
-        cusolverStatus_t s_ = (call);                                              \
-        if (s_ != CUSOLVER_STATUS_SUCCESS) {                                       \
-            set_error("cuSOLVER error %d in %s at %s:%d", (int)s_, #call, __FILE__, __LINE__); \
-            return CHPL_ERR_CUDA;                                                  \
-        }                                                                          \
-    } while (0)
 
 // CUDA call whose failure returns fin(status) (fin releases the caller's resources)
 #define CHPL_CUDA_OR(call, fin)                                                    \
@@ -112,17 +95,11 @@ struct Solver {
     int64_t N = 0, NB = 0, K = 0, ld = 0, ncols = 0;
     int agg = 1, nsm = 148, reserve = 0;
     cudaStream_t s0 = nullptr, sP = nullptr;  // bulk update (low priority), super-block chain (high priority)
-    cublasHandle_t hb0 = nullptr, hbP = nullptr;
-    cusolverDnHandle_t hs = nullptr;
-    cusolverDnParams_t hp = nullptr;
     double* A = nullptr;
-    int64_t* ipiv_rel = nullptr;
     int64_t* ipiv = nullptr;
     int* info = nullptr;
-    void* fwork_d = nullptr;
-    void* fwork_h = nullptr;
+    double* xwork = nullptr;               // back substitution scratch (N)
     void* pwork = nullptr;                 // workspace of the FP64 panel kernel
-    size_t fwd = 0, fwh = 0;
     std::vector<void*> lw[2];              // laswp plans of the panels of a super-block, by super-block parity
     void* wA[2] = {nullptr, nullptr};      // residues of a super-block's L21 (k = K), by parity, shared by streams
     void* wAin = nullptr;                  // residues of a panel's L21 for the inner updates (k = NB), sP only
@@ -172,13 +149,6 @@ struct Solver {
             CHPL_CUDA(cudaStreamCreateWithPriority(&sP, cudaStreamNonBlocking, hi));
         else
             sP = s0;
-        CHPL_CUBLAS(cublasCreate(&hb0));
-        CHPL_CUBLAS(cublasSetStream(hb0, s0));
-        CHPL_CUBLAS(cublasCreate(&hbP));
-        CHPL_CUBLAS(cublasSetStream(hbP, sP));
-        CHPL_CUSOLVER(cusolverDnCreate(&hs));
-        CHPL_CUSOLVER(cusolverDnSetStream(hs, sP));
-        CHPL_CUSOLVER(cusolverDnCreateParams(&hp));
 
         const size_t bytesA = (size_t)ld * (size_t)ncols * sizeof(double);
         const int64_t mmax = std::max<int64_t>(N - NB, 0);
@@ -196,15 +166,15 @@ struct Solver {
         const size_t restP = std::max(rest0, tot_in - a_in);      // sP runs both k = K and k = NB updates
         size_t freeB = 0, totB = 0;
         CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
-        CHPL_CUSOLVER(cusolverDnXgetrf_bufferSize(hs, hp, N, NB, CUDA_R_64F, nullptr, ld, CUDA_R_64F, &fwd, &fwh));
         const int npl = (int)((K + NB - 1) / NB);
         const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0);
-        const size_t need = bytesA + ozbytes + fwd + 2 * npl * laswp_work_bytes(NB) + (size_t)(2 * N + 64) * 8 +
+        const size_t pbytes = panel_work_bytes(N, NB);
+        const size_t need = bytesA + ozbytes + pbytes + 2 * npl * laswp_work_bytes(NB) + (size_t)(3 * N + 64) * 8 +
                             ((size_t)768 << 20);
         if (cfg.verbose)
             std::printf("MEM PLAN: matrix %.2f GiB | oz2 work %.2f GiB | getrf %.3f GiB | total %.2f GiB vs free %.2f GiB"
                         " | K=%" PRId64 " (agg %d) reserve %d SMs\n",
-                        bytesA / 1073741824.0, ozbytes / 1073741824.0, fwd / 1073741824.0, need / 1073741824.0,
+                        bytesA / 1073741824.0, ozbytes / 1073741824.0, pbytes / 1073741824.0, need / 1073741824.0,
                         freeB / 1073741824.0, K, agg, reserve);
         if (need > freeB) {
             set_error("memory plan: need %.2f GiB, %.2f GiB free (reduce N or HPLS_AGG)", need / 1073741824.0,
@@ -212,13 +182,11 @@ struct Solver {
             return CHPL_ERR_WORKSPACE;
         }
         CHPL_CUDA(cudaMalloc((void**)&A, bytesA));
-        CHPL_CUDA(cudaMalloc((void**)&ipiv_rel, (size_t)NB * sizeof(int64_t)));
         CHPL_CUDA(cudaMalloc((void**)&ipiv, (size_t)N * sizeof(int64_t)));
         CHPL_CUDA(cudaMalloc((void**)&info, 64 * sizeof(int)));
         CHPL_CUDA(cudaMemset(info, 0, 64 * sizeof(int)));
-        CHPL_CUDA(cudaMalloc(&fwork_d, fwd ? fwd : 8));
-        fwork_h = std::malloc(fwh ? fwh : 8);
-        CHPL_CUDA(cudaMalloc(&pwork, panel_work_bytes(N, NB)));
+        CHPL_CUDA(cudaMalloc((void**)&xwork, (size_t)N * sizeof(double)));
+        CHPL_CUDA(cudaMalloc(&pwork, pbytes));
         for (int b = 0; b < 2; ++b) {
             lw[b].assign(npl, nullptr);
             for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw[b][p], laswp_work_bytes(NB)));
@@ -255,17 +223,11 @@ struct Solver {
             if (wA[b]) cudaFree(wA[b]);
             for (void* p : lw[b]) if (p) cudaFree(p);
         }
-        if (fwork_d) cudaFree(fwork_d);
         if (pwork) cudaFree(pwork);
-        std::free(fwork_h);
+        if (xwork) cudaFree(xwork);
         if (info) cudaFree(info);
         if (ipiv) cudaFree(ipiv);
-        if (ipiv_rel) cudaFree(ipiv_rel);
         if (A) cudaFree(A);
-        if (hp) cusolverDnDestroyParams(hp);
-        if (hs) cusolverDnDestroy(hs);
-        if (hbP) cublasDestroy(hbP);
-        if (hb0) cublasDestroy(hb0);
         if (sP && sP != s0) cudaStreamDestroy(sP);
         if (s0) cudaStreamDestroy(s0);
     }
@@ -281,26 +243,25 @@ struct Solver {
 
     // C[:, c0:c0+nc] -= L21 * U12 with L21 = A(r0:N, a0:a0+k), U12 = A(a0:a0+k, c0:c0+nc),
     // C = A(r0:N, ...).  wa: A part of the residues (split here when split_a).
-    int update(cudaStream_t st, cublasHandle_t hb, void* work, void* wa, bool split_a, int64_t r0, int64_t a0,
-               int64_t k, int64_t c0, int64_t nc, int grid_cap)
+    int update(cudaStream_t st, void* work, void* wa, bool split_a, int64_t r0, int64_t a0, int64_t k, int64_t c0,
+               int64_t nc, int grid_cap)
     {
-        return emu(st, hb, work, wa, split_a, N - r0, k, at(r0, a0), ld, a0, c0, nc, at(r0, c0), -1.0, 1.0, grid_cap);
+        return emu(st, work, wa, split_a, N - r0, k, at(r0, a0), ld, a0, c0, nc, at(r0, c0), -1.0, 1.0, grid_cap);
     }
 
     // C(mt x nc) = alpha * Am(mt x k) * A(a0:a0+k, c0:c0+nc) + beta * C, C at Cp (ld).
     // B is split completely before the GEMM kernel writes C, so C may alias B
     // when beta == 0 (the kernel never reads B or, with beta == 0, C).
-    int emu(cudaStream_t st, cublasHandle_t hb, void* work, void* wa, bool split_a, int64_t mt, int64_t k,
-            const double* Am, int64_t lda_m, int64_t a0, int64_t c0, int64_t nc, double* Cp, double alpha, double beta,
-            int grid_cap)
+    int emu(cudaStream_t st, void* work, void* wa, bool split_a, int64_t mt, int64_t k, const double* Am,
+            int64_t lda_m, int64_t a0, int64_t c0, int64_t nc, double* Cp, double alpha, double beta, int grid_cap)
     {
         if (nc <= 0 || mt <= 0 || k <= 0) return CHPL_OK;
         const double one = beta, mone = alpha;
         PhaseTimer::Rec r;
         if (!cfg.emulate) {
             CHPL_TRY(clk.begin(st, PH_UPD_FP64, r));
-            CHPL_CUBLAS(cublasDgemm_64(hb, CUBLAS_OP_N, CUBLAS_OP_N, mt, nc, k, &mone, Am, lda_m, at(a0, c0), ld, &one, Cp,
-                                       ld));
+            CHPL_TRY(dgemm(st, mt, nc, k, mone, Am, lda_m, at(a0, c0), ld, one, Cp, ld));
+            ++n_launch;
             CHPL_TRY(clk.end(st, r));
             return CHPL_OK;
         }
@@ -355,14 +316,13 @@ struct Solver {
         return CHPL_OK;
     }
 
-    int trsm(cudaStream_t st, cublasHandle_t hb, int64_t d0, int64_t kd, int64_t c0, int64_t nc)
+    int trsm(cudaStream_t st, int64_t d0, int64_t kd, int64_t c0, int64_t nc)
     {
         if (nc <= 0 || kd <= 0) return CHPL_OK;
-        const double one = 1.0;
         PhaseTimer::Rec r;
         CHPL_TRY(clk.begin(st, PH_TRSM, r));
-        CHPL_CUBLAS(cublasDtrsm_64(hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, kd, nc,
-                                   &one, at(d0, d0), ld, at(d0, c0), ld));
+        CHPL_TRY(dtrsm_llnu(st, kd, nc, at(d0, d0), ld, at(d0, c0), ld));
+        n_launch += dtrsm_launches(kd);
         CHPL_TRY(clk.end(st, r));
         return CHPL_OK;
     }
@@ -383,36 +343,30 @@ struct Solver {
             void* plan = lw[s & 1][p];
             PhaseTimer::Rec r;
             CHPL_TRY(clk.begin(sP, PH_PANEL, r));
-            if (cfg.panel_mode == 1) {
-                CHPL_CUSOLVER(cusolverDnXgetrf(hs, hp, N - jp, nb, CUDA_R_64F, at(jp, jp), ld, ipiv_rel, CUDA_R_64F,
-                                               fwork_d, fwd, fwork_h, fwh, info + 1));
-                CHPL_TRY(ipiv_to_abs(sP, ipiv_rel, nb, jp, ipiv + jp));
-            } else {
-                CHPL_TRY(panel_getrf(sP, N - jp, nb, at(jp, jp), (size_t)ld, ipiv + jp, jp, info + 1, pwork));
-                n_launch += 2 * ((nb + 15) / 16) * 2;
-            }
+            CHPL_TRY(panel_getrf(sP, N - jp, nb, at(jp, jp), (size_t)ld, ipiv + jp, jp, info + 1, pwork));
+            n_launch += 2 * ((nb + 15) / 16) * 2;
             CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, plan));
             n_launch += 2;
             CHPL_TRY(clk.end(sP, r));
             CHPL_TRY(laswp_cols(sP, plan, nb, J, jp - J));
             const int64_t c0 = jp + nb, nc = J + KJ - c0;
             CHPL_TRY(laswp_cols(sP, plan, nb, c0, nc));
-            CHPL_TRY(trsm(sP, hbP, jp, nb, c0, nc));
-            CHPL_TRY(update(sP, hbP, wP, wAin, true, jp + nb, jp, nb, c0, nc, cap));
+            CHPL_TRY(trsm(sP, jp, nb, c0, nc));
+            CHPL_TRY(update(sP, wP, wAin, true, jp + nb, jp, nb, c0, nc, cap));
         }
         return invert_l(s);
     }
 
     // trailing work of super-block s on columns [c0, c0+nc): interchanges and U12
-    int trailing_swap_trsm(cudaStream_t st, cublasHandle_t hb, int64_t s, int64_t c0, int64_t nc)
+    int trailing_swap_trsm(cudaStream_t st, int64_t s, int64_t c0, int64_t nc)
     {
         const int64_t J = sb_start(s), KJ = sb_width(s);
         for (int64_t p = 0; J + p * NB < J + KJ; ++p)
             CHPL_TRY(laswp_cols(st, lw[s & 1][p], std::min(NB, J + KJ - (J + p * NB)), c0, nc));
-        if (!emu_trsm) return trsm(st, hb, J, KJ, c0, nc);
+        if (!emu_trsm) return trsm(st, J, KJ, c0, nc);
         // U12 = inv(L) * A12 in place (beta = 0: the kernel writes C from residues only)
-        return emu(st, hb, st == s0 ? w0 : wP, wLinv[s & 1], false, KJ, KJ, Linv[s & 1], KJ, J, c0, nc, at(J, c0), 1.0,
-                   0.0, st == s0 ? cap_bulk_cur : cap_chain_cur);
+        return emu(st, st == s0 ? w0 : wP, wLinv[s & 1], false, KJ, KJ, Linv[s & 1], KJ, J, c0, nc, at(J, c0), 1.0, 0.0,
+                   st == s0 ? cap_bulk_cur : cap_chain_cur);
     }
 
     // inv(L) of super-block s (unit lower KJ x KJ at A(J, J)), then its residues
@@ -424,9 +378,8 @@ struct Solver {
         PhaseTimer::Rec r;
         CHPL_TRY(clk.begin(sP, PH_TRSM, r));
         CHPL_TRY(identity(sP, Li, KJ));
-        const double one = 1.0;
-        CHPL_CUBLAS(cublasDtrsm_64(hbP, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, KJ, KJ,
-                                   &one, at(J, J), ld, Li, KJ));
+        CHPL_TRY(dtrsm_llnu(sP, KJ, KJ, at(J, J), ld, Li, KJ));
+        n_launch += 1 + dtrsm_launches(KJ);
         CHPL_TRY(clk.end(sP, r));
         const oz2::Moduli* M = oz2::moduli(cfg.moduli);
         const oz2::Layout y = oz2::layout((size_t)KJ, 256, (size_t)KJ, cfg.moduli, true, false);
@@ -469,22 +422,23 @@ struct Solver {
             cap_bulk_cur = cap_bulk;
             cap_chain_cur = cap_prev;
             if (ev_head) CHPL_CUDA(cudaStreamWaitEvent(sP, ev_head, 0));
-            CHPL_TRY(trailing_swap_trsm(sP, hbP, s, c1, K1));
-            CHPL_TRY(update(sP, hbP, wP, wA[s & 1], true, c1, J, KJ, c1, K1, cap_prev));
+            CHPL_TRY(trailing_swap_trsm(sP, s, c1, K1));
+            CHPL_TRY(update(sP, wP, wA[s & 1], true, c1, J, KJ, c1, K1, cap_prev));
             const bool a_split = K1 > 0 && N - c1 > 0;
             CHPL_TRY(wait(s0, sP));
             cap_chain_cur = cap_chain;
             if (K1 > 0) CHPL_TRY(factor_superblock(s + 1, cap_chain));
-            CHPL_TRY(trailing_swap_trsm(s0, hb0, s, c2, ncols - c2));
-            CHPL_TRY(update(s0, hb0, w0, wA[s & 1], !a_split, c1, J, KJ, c2, K2, cap_bulk));
+            CHPL_TRY(trailing_swap_trsm(s0, s, c2, ncols - c2));
+            CHPL_TRY(update(s0, w0, wA[s & 1], !a_split, c1, J, KJ, c2, K2, cap_bulk));
             ev_head = event();
             CHPL_CUDA(cudaEventRecord(ev_head, s0));
-            CHPL_TRY(update(s0, hb0, w0, wA[s & 1], !a_split && K2 == 0, c1, J, KJ, c2 + K2, ncols - c2 - K2, cap_bulk));
+            CHPL_TRY(update(s0, w0, wA[s & 1], !a_split && K2 == 0, c1, J, KJ, c2 + K2, ncols - c2 - K2, cap_bulk));
         }
         CHPL_TRY(wait(s0, sP));
         PhaseTimer::Rec r;
         CHPL_TRY(clk.begin(s0, PH_SOLVE, r));
-        CHPL_CUBLAS(cublasDtrsv_64(hb0, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N, CUBLAS_DIAG_NON_UNIT, N, A, ld, at(0, N), 1));
+        CHPL_TRY(dtrsv_unn(s0, N, A, ld, at(0, N), xwork));
+        n_launch += dtrsv_launches(N);
         CHPL_TRY(clk.end(s0, r));
         return CHPL_OK;
     }
@@ -534,6 +488,7 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     if (cfg->N <= 0 || cfg->NB <= 0 || cfg->NB > 2048) { set_error("bad N/NB (NB must be in [1, 2048])"); return CHPL_ERR_INVALID; }
     if (cfg->agg < 0 || (int64_t)cfg->agg * cfg->NB > 16384) { set_error("agg * NB must be <= 16384"); return CHPL_ERR_INVALID; }
     if (cfg->P != 1 || cfg->Q != 1) { set_error("chpl_hpl_run drives one GPU; use the grid driver for P x Q > 1"); return CHPL_ERR_INVALID; }
+    if (cfg->panel_mode != 0) { set_error("panel_mode: only this library's FP64 panel kernel (0) is built"); return CHPL_ERR_UNSUPPORTED; }
     if (cfg->emulate && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
     if (Ab && (int64_t)ldab < cfg->N) { set_error("ldab < N"); return CHPL_ERR_INVALID; }
     if (cfg->generator != CHPL_GEN_CHPL && cfg->generator != CHPL_GEN_PHILOX) {

@@ -20,15 +20,15 @@
 // Every element still receives exactly the operations of the unblocked
 // right-looking algorithm (x = fma(-l, u, x), l = a * (1 / pivot)), in the
 // same order.  Records and flags are double-buffered by column parity.
-// The recursion's FP64 GEMM / TRSM steps are plain cuBLAS calls; interchanges
-// use the device-built net permutation of hpl_kernels.cu.
-#include <cublas_v2.h>
-
+// The recursion's FP64 TRSM / GEMM steps run on this library's DMMA kernels
+// (fp64.cu); interchanges use the device-built net permutation of
+// hpl_kernels.cu.
 #include <algorithm>
 #include <mutex>
 #include <vector>
 
 #include "common.cuh"
+#include "fp64.h"
 #include "hpl.h"
 
 namespace chpl {
@@ -271,7 +271,6 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
 // ---------------------------------------------------------------------------- host
 struct PanelHandles {
     int dev = -1;
-    cublasHandle_t hb = nullptr;
     int grid = 0;
 };
 
@@ -282,9 +281,7 @@ static int handles(cudaStream_t st, PanelHandles** out)
     int dev = 0;
     CHPL_CUDA(cudaGetDevice(&dev));
     if (g_ph.dev != dev) {
-        if (g_ph.hb) cublasDestroy(g_ph.hb);
         g_ph = PanelHandles();
-        if (cublasCreate(&g_ph.hb) != CUBLAS_STATUS_SUCCESS) { set_error("cublasCreate failed"); return CHPL_ERR_CUDA; }
         int nsm = 0, per = 0;
         CHPL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
         CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
@@ -295,7 +292,7 @@ static int handles(cudaStream_t st, PanelHandles** out)
         g_ph.grid = nsm;  // one CTA per SM: co-resident by construction
         g_ph.dev = dev;
     }
-    if (cublasSetStream(g_ph.hb, st) != CUBLAS_STATUS_SUCCESS) { set_error("cublasSetStream failed"); return CHPL_ERR_CUDA; }
+    (void)st;
     *out = &g_ph;
     return CHPL_OK;
 }
@@ -357,18 +354,9 @@ int rec(PanelCtx& c, double* A, int64_t lda, int64_t m, int64_t n, int64_t* ipiv
     // its interchanges on the right half (pivots are relative to base_row)
     CHPL_TRY(laswp_plan(c.st, ipiv, 0, n1, c.plan, base_row));
     CHPL_TRY(laswp_apply(c.st, A, (size_t)lda, n1, n2, n1, c.plan));
-    const double one = 1.0, mone = -1.0;
-    if (cublasDtrsm_64(c.h->hb, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_N, CUBLAS_DIAG_UNIT, n1, n2, &one, A,
-                       lda, A + n1 * lda, lda) != CUBLAS_STATUS_SUCCESS) {
-        set_error("panel: dtrsm failed");
-        return CHPL_ERR_CUDA;
-    }
-    if (m > n1 &&
-        cublasDgemm_64(c.h->hb, CUBLAS_OP_N, CUBLAS_OP_N, m - n1, n2, n1, &mone, A + n1, lda, A + n1 * lda, lda, &one,
-                       A + n1 + n1 * lda, lda) != CUBLAS_STATUS_SUCCESS) {
-        set_error("panel: dgemm failed");
-        return CHPL_ERR_CUDA;
-    }
+    // U12 = L11^-1 A12, then the Schur update A22 -= L21 U12
+    CHPL_TRY(dtrsm_llnu(c.st, n1, n2, A, lda, A + n1 * lda, lda));
+    if (m > n1) CHPL_TRY(dgemm(c.st, m - n1, n2, n1, -1.0, A + n1, lda, A + n1 * lda, lda, 1.0, A + n1 + n1 * lda, lda));
     // right half (rows n1..m), pivots written relative to base_row + n1 -> shift to base_row
     CHPL_TRY(rec(c, A + n1 + n1 * lda, lda, m - n1, n2, ipiv + n1, base_row + n1, info_off + (int)n1));
     // its interchanges on the left half

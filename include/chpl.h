@@ -191,7 +191,8 @@ int chpl_laswp(void *stream, double *A, size_t lda, int64_t ncols, int64_t k1, i
 
 /*
  * FP64 LU with partial pivoting of an m x n panel (m >= n), in place:
- * recursive, warp-shuffle pivot search.  ipiv (device, n entries) receives
+ * recursive (TRSM and Schur update on the FP64 kernels above), cooperative
+ * base kernel with a warp-shuffle pivot search.  ipiv (device, n entries) receives
  * 0-based pivot rows relative to the panel, LAPACK order.  info (device int)
  * receives 0 or the 1-based column of the first exact zero pivot.
  * Replaces cusolverDnXgetrf of the panel (src/chpl_single.cu:668-679).
@@ -199,6 +200,32 @@ int chpl_laswp(void *stream, double *A, size_t lda, int64_t ncols, int64_t k1, i
 size_t chpl_panel_getrf_work_bytes(int64_t m, int64_t n);
 int chpl_panel_getrf_f64(void *stream, int64_t m, int64_t n, double *A, size_t lda, int64_t *ipiv,
                          int *info, void *work);
+
+/*
+ * FP64 BLAS of this library (sm_100a kernels; DGEMM on the FP64 tensor path,
+ * mma.sync m16n8k8 .f64).  Column-major, device pointers, asynchronous on
+ * `stream`, deterministic (fixed reduction orders).  They replace the cuBLAS
+ * calls of the reference's solve path.
+ *
+ * C (m x n) = alpha * A (m x k) * B (k x n) + beta * C (beta == 0 never reads
+ * C; C must not overlap A or B).  Replaces cublasDgemm at
+ * src/chpl_single.cu:621-623 (native update) and 694-696 (inner panel
+ * update), src/chpl_p2.cu:1377-1381, 1669-1673, 1697-1700.
+ */
+int chpl_dgemm(void *stream, int64_t m, int64_t n, int64_t k, double alpha, const double *A, size_t lda,
+               const double *B, size_t ldb, double beta, double *C, size_t ldc);
+/* B (n x nrhs) = L^-1 B with L unit lower triangular (its upper part is not
+ * read).  Replaces cublasDtrsm at src/chpl_single.cu:689-691, 708-710 and
+ * src/chpl_p2.cu:1211-1220 (inv(L11) against the identity). */
+int chpl_dtrsm_llnu(void *stream, int64_t n, int64_t nrhs, const double *L, size_t ldl, double *B, size_t ldb);
+/* x (n) = U^-1 x with U upper triangular, non-unit diagonal; work: n doubles
+ * of device scratch.  Replaces cublasDtrsv at src/chpl_single.cu:724-725 (the
+ * back solve, a one-column trsm there) and src/chpl_p2.cu:1851. */
+int chpl_dtrsv_unn(void *stream, int64_t n, const double *U, size_t ldu, double *x, double *work);
+/* y (m) = alpha * A (m x n) * x + beta * y (beta == 0 never reads y).
+ * Replaces cublasDgemv at src/chpl_p2.cu:1870. */
+int chpl_dgemv(void *stream, int64_t m, int64_t n, double alpha, const double *A, size_t lda, const double *x,
+               double beta, double *y);
 
 /*
  * HPL scaled residual of x (device, N) for the generated N x (N+1) system

@@ -24,27 +24,29 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, P, Q, N, NB, out, env=None):
+def _worker(rank, world, port, P, Q, N, NB, out, env=None, opts=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     os.environ.update(env or {})
     from chpl_b200 import grid
     dist = grid.init_from_env(timeout_s=300)
     g = grid.Grid(P, Q, timeout_s=120)
-    r = g.run(hpl.Config(N=N, NB=NB, P=P, Q=Q, moduli=12), want_x=True)
+    o = dict(moduli=12, emulate=True)
+    o.update(opts or {})
+    r = g.run(hpl.Config(N=N, NB=NB, P=P, Q=Q, **o), want_x=True)
     g.close()
     out[rank] = (r.passed, r.resid, r.x)
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _run_spawned(P, Q, N, NB, env=None):
+def _run_spawned(P, Q, N, NB, env=None, opts=None):
     import torch.multiprocessing as mp
     world = P * Q
     ctx = mp.get_context("spawn")
     with ctx.Manager() as m:
         out = m.dict()
-        mp.start_processes(_worker, args=(world, _free_port(), P, Q, N, NB, out, env), nprocs=world, join=True,
+        mp.start_processes(_worker, args=(world, _free_port(), P, Q, N, NB, out, env, opts), nprocs=world, join=True,
                            start_method="spawn")
         return dict(out)
 
@@ -67,13 +69,31 @@ def test_grid_1x1_in_process(cuda):
     assert np.allclose(r.x, _reference_x(3000), rtol=1e-6, atol=1e-8)
 
 
+def test_grid_1x1_fp64_update(cuda):
+    """CHPL2D_G8=0 (the reference's compiled-in default): the trailing update
+    and U12 run in FP64 on the library's DGEMM, on the serial block steps."""
+    import torch.distributed as dist
+    from chpl_b200 import grid
+    if not dist.is_initialized():
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    g = grid.Grid(1, 1)
+    r = g.run(hpl.Config(N=3000, NB=512, P=1, Q=1, emulate=False), want_x=True)
+    g.close()
+    assert r.passed and r.resid < 1.0, r.resid
+    assert np.allclose(r.x, _reference_x(3000), rtol=1e-9, atol=1e-11)
+
+
+@pytest.mark.parametrize("moduli", [11, 12])
 @pytest.mark.parametrize("grid_shape", [(1, 2), (2, 1)])
-def test_grid_two_ranks(cuda, grid_shape):
+def test_grid_two_ranks(cuda, grid_shape, moduli):
+    """Two ranks at the benchmark's 11 moduli and at 12, against the FP64
+    solution of the same system."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     P, Q = grid_shape
     N, NB = 4000, 256
-    out = _run_spawned(P, Q, N, NB)
+    out = _run_spawned(P, Q, N, NB, opts={"moduli": moduli})
     xs = _reference_x(N)
     for rank in range(P * Q):
         passed, resid, x = out[rank]
@@ -81,10 +101,26 @@ def test_grid_two_ranks(cuda, grid_shape):
         assert np.allclose(x, xs, rtol=1e-6, atol=1e-8)
 
 
-def test_grid_2x2(cuda):
+@pytest.mark.parametrize("grid_shape", [(1, 2), (2, 1)])
+def test_grid_two_ranks_fp64_update(cuda, grid_shape):
+    """CHPL2D_G8=0 on two ranks: FP64 update, serial block steps."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    P, Q = grid_shape
+    N, NB = 4000, 256
+    out = _run_spawned(P, Q, N, NB, opts={"emulate": False})
+    xs = _reference_x(N)
+    for rank in range(P * Q):
+        passed, resid, x = out[rank]
+        assert passed and resid < 1.0, resid
+        assert np.allclose(x, xs, rtol=1e-9, atol=1e-11)
+
+
+@pytest.mark.parametrize("moduli", [11, 12])
+def test_grid_2x2(cuda, moduli):
     if torch.cuda.device_count() < 4:
         pytest.skip("needs 4 GPUs")
-    out = _run_spawned(2, 2, 5000, 256)
+    out = _run_spawned(2, 2, 5000, 256, opts={"moduli": moduli})
     xs = _reference_x(5000)
     for rank in range(4):
         passed, resid, x = out[rank]

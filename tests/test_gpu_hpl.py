@@ -173,13 +173,20 @@ def test_hpl_ragged_sizes(cuda):
     assert res.passed, res.resid
 
 
-def test_hpl_panel_kernel_matches_cusolver_pivots(cuda):
-    """Own FP64 panel kernel vs cuSOLVER getrf inside the solver: same pivots, so
-    the same solution up to rounding."""
-    a = hpl.run(hpl.Config(N=3000, NB=512, moduli=12, panel_mode=0), want_x=True)
-    b = hpl.run(hpl.Config(N=3000, NB=512, moduli=12, panel_mode=1), want_x=True)
-    assert a.passed and b.passed
-    assert np.allclose(a.x, b.x, rtol=1e-6, atol=1e-9)
+def test_hpl_fp64_solve_matches_lapack(cuda):
+    """The all-FP64 solve (own panel kernel, own TRSM / DGEMM / TRSV, no
+    emulation) against LAPACK's solve of the same generated system."""
+    N = 3000
+    a = hpl.run(hpl.Config(N=N, NB=512, emulate=False), want_x=True)
+    assert a.passed, a.resid
+    x = oracle.lapack_hpl_solve(np.asfortranarray(oracle.hpl_system(N)))
+    assert np.allclose(a.x, x, rtol=1e-9, atol=1e-11)
+    assert a.resid < 1.0
+
+
+def test_hpl_rejects_other_panel_modes(cuda):
+    with pytest.raises(_lib.ChplError):
+        hpl.run(hpl.Config(N=512, NB=128, panel_mode=1))
 
 
 def test_hpl_emulated_vs_oracle_small(cuda):

@@ -81,7 +81,8 @@ def test_grid_1x1_fp64_update(cuda):
     r = g.run(hpl.Config(N=3000, NB=512, P=1, Q=1, emulate=False), want_x=True)
     g.close()
     assert r.passed and r.resid < 1.0, r.resid
-    assert np.allclose(r.x, _reference_x(3000), rtol=1e-9, atol=1e-11)
+    # forward error of two backward-stable solves of a system with condition ~1e5
+    assert np.allclose(r.x, _reference_x(3000), rtol=1e-7, atol=1e-9)
 
 
 @pytest.mark.parametrize("moduli", [11, 12])
@@ -113,7 +114,7 @@ def test_grid_two_ranks_fp64_update(cuda, grid_shape):
     for rank in range(P * Q):
         passed, resid, x = out[rank]
         assert passed and resid < 1.0, resid
-        assert np.allclose(x, xs, rtol=1e-9, atol=1e-11)
+        assert np.allclose(x, xs, rtol=1e-7, atol=1e-9)
 
 
 @pytest.mark.parametrize("moduli", [11, 12])

@@ -180,7 +180,8 @@ def test_hpl_fp64_solve_matches_lapack(cuda):
     a = hpl.run(hpl.Config(N=N, NB=512, emulate=False), want_x=True)
     assert a.passed, a.resid
     x = oracle.lapack_hpl_solve(np.asfortranarray(oracle.hpl_system(N)))
-    assert np.allclose(a.x, x, rtol=1e-9, atol=1e-11)
+    # forward error of two backward-stable solves of a system with condition ~1e5
+    assert np.allclose(a.x, x, rtol=1e-7, atol=1e-9)
     assert a.resid < 1.0
 
 

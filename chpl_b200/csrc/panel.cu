@@ -134,15 +134,19 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
                 const int oq = __shfl_xor_sync(0xffffffffu, q, o);
                 if (better(ov, orr, v, r)) { v = ov; r = orr; q = oq; }
             }
-            PanelRec* rec = recs + (size_t)(jc & 1) * G + blockIdx.x;
-            if (lane < w) {
-                if (v >= 0.0) rec->cand[lane] = stage[q][lane];
-                if (blockIdx.x == 0) rec->top[lane] = stage_top[lane];
+            // one writer: the record in program order, then the flag with release semantics
+            // (no separate fence: a release store orders its own thread's earlier stores)
+            if (lane == 0) {
+                PanelRec* rec = recs + (size_t)(jc & 1) * G + blockIdx.x;
+                if (v >= 0.0)
+                    for (int c = 0; c < w; c += 2)
+                        *reinterpret_cast<double2*>(&rec->cand[c]) = make_double2(stage[q][c], stage[q][c + 1]);
+                if (blockIdx.x == 0)
+                    for (int c = 0; c < w; c += 2)
+                        *reinterpret_cast<double2*>(&rec->top[c]) = make_double2(stage_top[c], stage_top[c + 1]);
+                *reinterpret_cast<double2*>(rec) = make_double2(v, __longlong_as_double(r));
+                st_release(&flags[blockIdx.x], sbase + (unsigned int)jc + 1u);
             }
-            if (lane == 0) { rec->val = v; rec->row = r; }
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release(&flags[blockIdx.x], sbase + (unsigned int)jc + 1u);
         }
     };
 
@@ -175,6 +179,9 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
             }
             return true;
         };
+        // threads [0, G) fetch the CTAs' records, threads [kTopT, kTopT + w) the diagonal
+        // row from CTA 0's record, both at once
+        constexpr int kTopT = kPanelThreads - W;
         if (tid < G) {
             good = poll(tid) ? 1 : 0;
             if (good) {  // the whole record in one round trip
@@ -191,8 +198,8 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
                 }
             }
         }
-        if (tid < w && good) {  // the diagonal row, one element per thread, from CTA 0's record
-            if (tid == 0 || poll(0)) tv[tid] = __ldcg(&(recs + (size_t)(j & 1) * G)->top[tid]);
+        if (tid >= kTopT && tid - kTopT < w) {  // the diagonal row, one element per thread
+            if (poll(0)) tv[tid - kTopT] = __ldcg(&(recs + (size_t)(j & 1) * G)->top[tid - kTopT]);
             else good = 0;
         }
         int t = tid;
@@ -327,6 +334,10 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
     const int G = (int)std::max<int64_t>(1, std::min<int64_t>(c.h->grid, (m + rows_fit - 1) / rows_fit));
     const int64_t rows_per = (m + G - 1) / G;
     const size_t smem = (size_t)rows_per * w * sizeof(double);
+    if (G > kPanelThreads - kBaseW) {   // the record fetchers and the diagonal-row fetchers must not overlap
+        set_error("panel: %d CTAs exceed the exchange's %d record threads", G, kPanelThreads - kBaseW);
+        return CHPL_ERR_UNSUPPORTED;
+    }
     if (smem > (size_t)kSmemBytes) {
         set_error("panel of %lld rows x %d columns exceeds the on-chip capacity", (long long)m, w);
         return CHPL_ERR_UNSUPPORTED;

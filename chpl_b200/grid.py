@@ -100,7 +100,8 @@ def max_over_ranks(v: float) -> float:
     return float(t.item())
 
 
-def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffic_per_unit=None) -> None:
+def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffic_per_unit=None,
+          fp64_peak_tflops=None) -> None:
     """bench.py for N > 1 GPUs (driver contract): weak scaling, max over ranks."""
     import torch
     dist = init_from_env()
@@ -147,6 +148,7 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
     # the cuBLAS int8 denominator, measured after the solves (whose memory plan wants every free byte),
     # by every rank on its own GPU
     peak_burst, peak = int8_peak_tops(sustained_s=4.0) if int8_peak_tops else (None, None)
+    fp64_peak = fp64_peak_tflops() if fp64_peak_tflops else None
     g.close()
     if rank == 0:
         out = {
@@ -182,6 +184,10 @@ def bench(a, workloads, metric, flops, ClockSampler, int8_peak_tops=None, traffi
                     "note": "public API chpl_grid_run per step (wall clock, max over ranks): on-device "
                             "block-cyclic generation of the HPL system, solve, verification, x to the host; "
                             "no host copy of the ranks' local pieces (~144 GB each) is made"},
+            "fp64_native": ({"peak_tflops_per_gpu": fp64_peak,
+                             "x_peak_per_gpu": a.steps * flops(N) / solve / 1e12 / world / fp64_peak,
+                             "source": "cuBLAS DGEMM 8192^3 (torch.matmul float64) on rank 0's GPU, this run"}
+                            if fp64_peak else None),
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }

@@ -258,6 +258,37 @@ __global__ void __launch_bounds__(kLeafThreads) trsm_leaf_kernel(int n, const do
         if (i < n) col[i] = x[i];
 }
 
+// The same solve with one warp per right-hand side (two rows per lane, x_j
+// broadcast by shuffle), for few right-hand sides: the panel recursion's
+// solves have 256-512 of them, which one thread each would spread over only
+// 2-4 CTAs.
+constexpr int kLeafWarps = 8;
+
+__global__ void __launch_bounds__(kLeafWarps * 32) trsm_leaf_warp_kernel(int n, const double* __restrict__ L,
+                                                                        long long ldl, double* __restrict__ B,
+                                                                        long long ldb, long long nrhs)
+{
+    __shared__ double Ls[kLeaf][kLeaf + 1];   // Ls[j][i] = L(i, j)
+    for (int e = threadIdx.x; e < kLeaf * kLeaf; e += blockDim.x) {
+        const int i = e % kLeaf, j = e / kLeaf;
+        Ls[j][i] = (i < n && j < n && i > j) ? L[i + j * ldl] : 0.0;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const long long c = (long long)blockIdx.x * kLeafWarps + (threadIdx.x >> 5);
+    if (c >= nrhs) return;
+    double* col = B + c * ldb;
+    double r0 = lane < n ? col[lane] : 0.0;
+    double r1 = lane + 32 < n ? col[lane + 32] : 0.0;
+    for (int j = 0; j < n; ++j) {
+        const double xj = __shfl_sync(0xffffffffu, j < 32 ? r0 : r1, j & 31);
+        r0 = fma(-Ls[j][lane], xj, r0);          // Ls[j][i] = 0 for i <= j: rows at or above j keep their value
+        r1 = fma(-Ls[j][lane + 32], xj, r1);
+    }
+    if (lane < n) col[lane] = r0;
+    if (lane + 32 < n) col[lane + 32] = r1;
+}
+
 // ---------------------------------------------------------------------------- TRSV
 // Upper triangular solve by blocks of kTrsvB rows from the bottom, one kernel
 // per block j.  Every CTA first solves the diagonal block itself (one warp,
@@ -347,10 +378,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(long long m, long
 int trsm_rec(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_t ldl, double* B, int64_t ldb)
 {
     if (n <= kLeaf) {
-        const long long g = (nrhs + kLeafThreads - 1) / kLeafThreads;
-        if (g > 0x7fffffffLL) { set_error("dtrsm: too many right-hand sides"); return CHPL_ERR_UNSUPPORTED; }
-        trsm_leaf_kernel<<<(unsigned)g, kLeafThreads, 0, st>>>((int)n, L, (long long)ldl, B, (long long)ldb,
-                                                               (long long)nrhs);
+        if (nrhs < 32768) {   // few right-hand sides: a warp each
+            const long long g = (nrhs + kLeafWarps - 1) / kLeafWarps;
+            trsm_leaf_warp_kernel<<<(unsigned)g, kLeafWarps * 32, 0, st>>>((int)n, L, (long long)ldl, B, (long long)ldb,
+                                                                           (long long)nrhs);
+        } else {
+            const long long g = (nrhs + kLeafThreads - 1) / kLeafThreads;
+            if (g > 0x7fffffffLL) { set_error("dtrsm: too many right-hand sides"); return CHPL_ERR_UNSUPPORTED; }
+            trsm_leaf_kernel<<<(unsigned)g, kLeafThreads, 0, st>>>((int)n, L, (long long)ldl, B, (long long)ldb,
+                                                                   (long long)nrhs);
+        }
         CHPL_CUDA(cudaGetLastError());
         return CHPL_OK;
     }

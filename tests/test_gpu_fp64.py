@@ -89,7 +89,8 @@ def _unit_lower(n, rng):
     return L
 
 
-@pytest.mark.parametrize("n,nrhs", [(1, 1), (63, 5), (64, 130), (65, 64), (200, 513), (1000, 1000), (4096, 300)])
+@pytest.mark.parametrize("n,nrhs", [(1, 1), (63, 5), (64, 130), (65, 64), (200, 513), (1000, 1000), (4096, 300),
+                                    (100, 40000)])
 def test_dtrsm_matches_scipy(cuda, n, nrhs):
     rng = np.random.default_rng(n + nrhs)
     L = _unit_lower(n, rng)

@@ -370,6 +370,40 @@ struct Emu {
     }
 };
 
+// ---------------------------------------------------------------------------- per-phase stream time
+// Busy time of one stream between two events, summed per phase (the indices
+// of chpl_hpl_result.phase_s: 0 panel, 1 interchanges, 2 U12, 3 split of W,
+// 4 update, 6 back substitution, 7 broadcasts).  Streams overlap, so the
+// phases of a lookahead step add up to more than its wall time.
+struct PhaseEvents {
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> recs;
+    cudaEvent_t begin(cudaStream_t s)
+    {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreate(&e) == cudaSuccess) cudaEventRecord(e, s);
+        return e;
+    }
+    void end(cudaStream_t s, int ph, cudaEvent_t e0)
+    {
+        cudaEvent_t e1 = nullptr;
+        if (!e0 || cudaEventCreate(&e1) != cudaSuccess) return;
+        cudaEventRecord(e1, s);
+        recs.push_back({ph, {e0, e1}});
+    }
+    void collect(double* out)
+    {
+        for (auto& r : recs) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, r.second.first, r.second.second) == cudaSuccess) out[r.first] += ms * 1e-3;
+            cudaEventDestroy(r.second.first);
+            cudaEventDestroy(r.second.second);
+        }
+        recs.clear();
+    }
+    ~PhaseEvents() { collect(sink); }
+    double sink[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+};
+
 // ---------------------------------------------------------------------------- grid solver
 struct GridSolver {
     GridComm* g = nullptr;
@@ -414,6 +448,7 @@ struct GridSolver {
     Emu emu;
     int64_t n_launch = 0;
     double phase[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    PhaseEvents pev;               // stream-busy phases of the lookahead schedules and the back substitution
     static constexpr int64_t kXchCols = 4096;
 
     // the two W slots (mloc x NB each) and the gathered panel ((N - J) x NB at most) share Wd
@@ -824,15 +859,22 @@ struct GridSolver {
     {
         if (nc <= 0) return CHPL_OK;
         const int64_t J = s * NB, K = Kof(s), mW = N - J - K;
+        cudaEvent_t t = pev.begin(st);
         for (int64_t k0 = 0; k0 < K; k0 += kPlanSwaps) {   // the block's swaps in order, one plan per chunk
             const void* pl = static_cast<uint8_t*>(plan2) + (k0 / kPlanSwaps) * round_up(laswp_work_bytes(kPlanSwaps), 256);
             CHPL_TRY(laswp_apply(st, A + J, (size_t)lda, c0, nc, std::min(kPlanSwaps, K - k0), pl));
             ++n_launch;
         }
+        pev.end(st, 1, t);
+        t = pev.begin(st);
         CHPL_TRY(emu.run(st, wlinv, true, K, nc, K, lv, K, A + J + c0 * lda, lda, A + J + c0 * lda, lda, 1.0, 0.0));
-        if (mW > 0)
+        pev.end(st, 2, t);
+        if (mW > 0) {
+            t = pev.begin(st);
             CHPL_TRY(emu.run(st, wres, false, mW, nc, K, arena, mW, A + J + c0 * lda, lda, A + J + K + c0 * lda, lda, -1.0,
                              1.0));
+            pev.end(st, 4, t);
+        }
         return CHPL_OK;
     }
 
@@ -867,17 +909,21 @@ struct GridSolver {
                 if (evWfree) cudaStreamWaitEvent(sm, evWfree, 0);
                 if (evLfree[slot]) cudaStreamWaitEvent(sm, evLfree[slot], 0);
             }
+            cudaEvent_t tb = pev.begin(sm);
             ncclGroupStart();
             ncclBroadcast(Pv[slot], Pv[slot], (size_t)K, ncclInt64, qs, g->row, sm);
             ncclBroadcast(Lv[slot], Lv[slot], (size_t)K * K, ncclDouble, qs, g->row, sm);
             if (mW > 0) ncclBroadcast(arena, arena, (size_t)mW * K, ncclDouble, qs, g->row, sm);
             if (ncclGroupEnd() != ncclSuccess) { set_error("NCCL broadcast of block %lld failed", (long long)s); rc = CHPL_ERR_NCCL; break; }
+            pev.end(sm, 7, tb);
             cudaEvent_t evW;
             if ((rc = mk(&evW)) != CHPL_OK) break;
             cudaEventRecord(evW, sm);
             // ---- computation ----
             cudaStreamWaitEvent(st, evW, 0);
+            cudaEvent_t ts = pev.begin(st);
             if ((rc = emu.split_only(st, wres, mW, K, arena, mW)) != CHPL_OK) break;
+            pev.end(st, 3, ts);
             if ((rc = mk(&evWfree)) != CHPL_OK) break;
             cudaEventRecord(evWfree, st);
             const int64_t tc0 = local_extent(J + K, NB, Q, qc), ntr = nloc - tc0;
@@ -1119,6 +1165,7 @@ struct GridSolver {
                 if (lfree_rec[slot]) cudaStreamWaitEvent(sm, evLfree[slot], 0);
                 if (g_rec) cudaStreamWaitEvent(sm, evG, 0);
             }
+            cudaEvent_t tb = pev.begin(sm);
             ncclGroupStart();
             ncclBroadcast(Pv[slot], Pv[slot], (size_t)K, ncclInt64, 2 * qs + ps, g->world, sm);
             if (ncclGroupEnd() != ncclSuccess) { rc = CHPL_ERR_NCCL; set_error("pivot broadcast failed"); break; }
@@ -1126,12 +1173,15 @@ struct GridSolver {
             if (pr == ps) ncclBroadcast(Lv[slot], Lv[slot], (size_t)K * K, ncclDouble, qs, g->row, sm);
             if (mW > 0) ncclBroadcast(Wslot, Wslot, (size_t)mW * K, ncclDouble, qs, g->row, sm);
             if (ncclGroupEnd() != ncclSuccess) { rc = CHPL_ERR_NCCL; set_error("W broadcast failed"); break; }
+            pev.end(sm, 7, tb);
             cudaEventRecord(evA, sm);
             cudaMemcpyAsync(hpiv + (size_t)slot * NB, Pv[slot], (size_t)K * sizeof(int64_t), cudaMemcpyDeviceToHost, sm);
             cudaEventRecord(evPH, sm);
             // ---- computation ----
             cudaStreamWaitEvent(st, evA, 0);
+            cudaEvent_t ts = pev.begin(st);
             if ((rc = emu.split_only(st, wres, mW, K, Wslot, mW)) != CHPL_OK) break;
+            pev.end(st, 3, ts);
             cudaEventRecord(evWfree[slot], st);
             wfree_rec[slot] = true;
             if ((rc = watchdog_event(g, evPH, "pivots")) != CHPL_OK) break;
@@ -1150,26 +1200,38 @@ struct GridSolver {
             const bool chain = s + 1 < nblk && qc == q1;
             const int64_t urg = chain ? std::min<int64_t>(Kof(s + 1), ntr) : 0;
             if (chain) {   // block s+1 first: interchanges, U12, update, then its factorization
+                cudaEvent_t t = pev.begin(st);
                 if ((rc = exchange2(tc0, urg, DL[slot], Ls, sm, g->col, e1, e2)) != CHPL_OK) break;
+                pev.end(st, 1, t);
                 double* Us = Uu + (size_t)slot * NB * NB;
+                t = pev.begin(st);
                 if ((rc = u12(s, tc0, urg, Lv[slot], Us, sm, g->col, e1, e2)) != CHPL_OK) break;
+                pev.end(st, 2, t);
+                t = pev.begin(st);
                 if (mW > 0 &&
                     (rc = emu.run(st, wres, false, mW, urg, K, Wslot, mW, Us, K, A + lrw + tc0 * lda, lda, -1.0, 1.0)) !=
                         CHPL_OK)
                     break;
+                pev.end(st, 4, t);
                 if ((rc = chain_factor(s + 1, tc0, Pv[slot ^ 1], Lv[slot ^ 1], evF, evG, e1, e2)) != CHPL_OK) break;
                 g_rec = true;
             }
             // ---- the rest of the columns ----
             const int64_t c0 = tc0 + urg, nc = ntr - urg;
+            cudaEvent_t tx = pev.begin(st);
             if ((rc = exchange2(c0, nc, DL[slot], Ls, sb, g->col2, e3, e4)) != CHPL_OK) break;
+            pev.end(st, 1, tx);
             if (nc > 0) {
                 if (s > 0) cudaStreamWaitEvent(sb, evEnd[slot ^ 1], 0);   // Ub is free (read by step s-1's update)
+                cudaEvent_t t = pev.begin(st);
                 if ((rc = u12(s, c0, nc, Lv[slot], Ub, sb, g->col2, e3, e4)) != CHPL_OK) break;
+                pev.end(st, 2, t);
+                t = pev.begin(st);
                 if (mW > 0 &&
                     (rc = emu.run(st, wres, false, mW, nc, K, Wslot, mW, Ub, K, A + lrw + c0 * lda, lda, -1.0, 1.0)) !=
                         CHPL_OK)
                     break;
+                pev.end(st, 4, t);
             }
             cudaEventRecord(evLfree[slot], st);
             lfree_rec[slot] = true;
@@ -1193,6 +1255,7 @@ struct GridSolver {
         const int P = g->P, Q = g->Q, pr = g->pr, qc = g->qc;
         const int qN = (int)((N / NB) % Q);
         const int64_t lcN = local_extent(N, NB, Q, qN);
+        cudaEvent_t tbs = pev.begin(st);
         CHPL_CUDA(cudaMemsetAsync(tsum, 0, (size_t)std::max<int64_t>(mloc, 1) * 8, st));
         CHPL_CUDA(cudaMemsetAsync(x, 0, (size_t)N * 8, st));
         for (int64_t j = nblk - 1; j >= 0; --j) {
@@ -1222,6 +1285,7 @@ struct GridSolver {
             }
         }
         if (g->P * g->Q > 1) CHPL_NCCL(ncclAllReduce(x, x, (size_t)N, ncclDouble, ncclSum, g->world, st));
+        pev.end(st, 6, tbs);
         return watchdog_sync(g, st, "back substitution");
     }
 
@@ -1314,10 +1378,17 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     res->passed = hinfo == 0 && std::isfinite(res->resid) && res->resid < cfg->threshold;
     s.emu.collect();
     res->schedule = s.la || s.la2 ? 1 : 0;
+    // serial block steps: wall time of each step's phases (host clock); lookahead: stream-busy time of each
+    // phase (device events), plus the panel factorizations (device events) in phase 0 either way
+    double pe[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    s.pev.collect(pe);
     res->phase_s[0] = s.phase[0];
-    res->phase_s[1] = s.phase[1];
-    res->phase_s[2] = s.phase[2];
-    res->phase_s[4] = s.phase[3];
+    res->phase_s[1] = s.la || s.la2 ? pe[1] : s.phase[1];
+    res->phase_s[2] = s.la || s.la2 ? pe[2] : s.phase[2];
+    res->phase_s[3] = pe[3];
+    res->phase_s[4] = s.la || s.la2 ? pe[4] : s.phase[3];
+    res->phase_s[6] = pe[6];
+    res->phase_s[7] = pe[7];
     res->gemm_launches = s.emu.gemm_n;
     res->gemm_kernel_s = s.emu.kernel_s;
     res->gemm_int8_ops = s.emu.ops;

@@ -3,6 +3,9 @@
     python -m chpl_b200.cases gemm --m 32768 --n 32768 --k 4096 --moduli 11 [--reps 3]
     python -m chpl_b200.cases hpl --N 65536 --NB 1024 [--no-lookahead]
     python -m chpl_b200.cases laswp --rows 139264 --cols 65536 --swaps 1024
+    python -m chpl_b200.cases panel --m 139264 --n 1024
+    python -m chpl_b200.cases dgemm --m 8192 --n 8192 --k 8192   (FP64 DGEMM, beside cuBLAS's)
+    python -m chpl_b200.cases trsm --m 139264 --n 1024           (m right-hand sides)
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m chpl_b200.cases grid --N 131072 --NB 2048 --moduli 11 12
 
 Prints one JSON line per case.  Inputs are uniform [-0.5, 0.5) (the
@@ -55,6 +58,45 @@ def gemm_case(m: int, n: int, k: int, L: int, reps: int, scaled: bool, sustain: 
         out["sustained"] = {"iters": n_it, "s": ts, "fp64eq_tflops": n_it * 2.0 * m * n * k / ts / 1e12,
                             "clocks": clk.summary()}
     return out
+
+
+def fp64_case(what: str, m: int, n: int, k: int, reps: int) -> dict:
+    """This library's FP64 DGEMM (m x n x k, C -= A B) or TRSM (n x n unit
+    lower against m right-hand sides) beside cuBLAS's on the same operands
+    (torch), best of `reps`, CUDA events."""
+    from . import _lib
+    L = _lib.load()
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        best = 1e30
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e-3)
+        return best
+
+    if what == "dgemm":
+        A = torch.rand(k, m, dtype=torch.float64, device="cuda").t()   # column-major m x k
+        B = torch.rand(n, k, dtype=torch.float64, device="cuda").t()
+        C = torch.rand(n, m, dtype=torch.float64, device="cuda").t()
+        t = timed(lambda: _lib.check(L.chpl_dgemm(None, m, n, k, -1.0, A.data_ptr(), m, B.data_ptr(), k, 1.0,
+                                                  C.data_ptr(), m), "chpl_dgemm"))
+        tc = timed(lambda: C.addmm_(A, B, alpha=-1.0))
+        f = 2.0 * m * n * k
+        return {"case": "dgemm", "m": m, "n": n, "k": k, "ms": t * 1e3, "tflops": f / t / 1e12,
+                "cublas_ms": tc * 1e3, "cublas_tflops": f / tc / 1e12}
+    Lm = torch.rand(n, n, dtype=torch.float64, device="cuda") / n     # column-major; unit lower part used
+    Bm = torch.rand(m, n, dtype=torch.float64, device="cuda")          # n x m right-hand sides
+    t = timed(lambda: _lib.check(L.chpl_dtrsm_llnu(None, n, m, Lm.data_ptr(), n, Bm.data_ptr(), n), "chpl_dtrsm"))
+    Lt = torch.tril(Lm.t(), -1) + torch.eye(n, dtype=torch.float64, device="cuda")
+    Bt = Bm.t().contiguous()
+    tc = timed(lambda: torch.linalg.solve_triangular(Lt, Bt, upper=False, unitriangular=True))
+    return {"case": "trsm", "n": n, "nrhs": m, "ms": t * 1e3, "tflops": n * n * m / t / 1e12, "cublas_ms": tc * 1e3}
 
 
 def panel_case(m: int, n: int, reps: int) -> dict:
@@ -167,6 +209,12 @@ def main() -> None:
     g.add_argument("--reps", type=int, default=3)
     g.add_argument("--scaled", action="store_true")
     g.add_argument("--sustain", type=float, default=0.0, help="also run back to back for this many seconds")
+    for nm in ("dgemm", "trsm"):
+        f = sub.add_parser(nm)
+        f.add_argument("--m", type=int, default=8192, help="rows (dgemm) / right-hand sides (trsm)")
+        f.add_argument("--n", type=int, default=8192)
+        f.add_argument("--k", type=int, default=8192)
+        f.add_argument("--reps", type=int, default=5)
     pn = sub.add_parser("panel")
     pn.add_argument("--m", type=int, default=65536)
     pn.add_argument("--n", type=int, default=1024)
@@ -199,6 +247,8 @@ def main() -> None:
     torch.cuda.set_device(0)
     if a.what == "gemm":
         print(json.dumps(gemm_case(a.m, a.n, a.k, a.moduli, a.reps, a.scaled, a.sustain)), flush=True)
+    elif a.what in ("dgemm", "trsm"):
+        print(json.dumps(fp64_case(a.what, a.m, a.n, a.k, a.reps)), flush=True)
     elif a.what == "panel":
         print(json.dumps(panel_case(a.m, a.n, a.reps)), flush=True)
     elif a.what == "laswp":

@@ -298,7 +298,9 @@ __global__ void __launch_bounds__(kLeafWarps * 32) trsm_leaf_warp_kernel(int n, 
 // separate buffer (CTA 0 writes them), so no CTA overwrites rows another CTA
 // of the same kernel still reads; the caller copies the buffer back.
 constexpr int kTrsvB = 64;
-constexpr int kTrsvThreads = 256;   // rows per CTA of the update
+constexpr int kTrsvRows = 64;       // rows per CTA of the update
+constexpr int kTrsvGroups = 4;      // column groups per row: 16 independent loads per thread
+constexpr int kTrsvThreads = kTrsvRows * kTrsvGroups;
 
 __global__ void __launch_bounds__(kTrsvThreads) trsv_block_kernel(const double* __restrict__ U, long long ldu,
                                                                  double* __restrict__ x, double* __restrict__ xout,
@@ -306,6 +308,7 @@ __global__ void __launch_bounds__(kTrsvThreads) trsv_block_kernel(const double* 
 {
     __shared__ double Us[kTrsvB][kTrsvB + 1];   // Us[c][r] = U(j0 + r, j0 + c)
     __shared__ double xs[kTrsvB];
+    __shared__ double part[kTrsvGroups][kTrsvRows];
     const int tid = threadIdx.x, lane = tid & 31;
     for (int e = tid; e < b * b; e += blockDim.x) {
         const int i = e % b, j = e / b;
@@ -325,22 +328,27 @@ __global__ void __launch_bounds__(kTrsvThreads) trsv_block_kernel(const double* 
             if (lane < i) r0 = fma(-Us[i][lane], xi, r0);
             if (lane + 32 < i) r1 = fma(-Us[i][lane + 32], xi, r1);
         }
-        if (lane < b) xs[lane] = r0;
-        if (lane + 32 < b) xs[lane + 32] = r1;
+        xs[lane] = lane < b ? r0 : 0.0;
+        xs[lane + 32] = lane + 32 < b ? r1 : 0.0;
     }
     __syncthreads();
     if (blockIdx.x == 0 && tid < b) xout[j0 + tid] = xs[tid];
-    const long long r = (long long)blockIdx.x * kTrsvThreads + tid;
-    if (r >= j0) return;
-    const double* u = U + r + j0 * ldu;
-    double s0 = 0.0, s1 = 0.0;
-    int c = 0;
-    for (; c + 1 < b; c += 2) {
-        s0 = fma(u[c * ldu], xs[c], s0);
-        s1 = fma(u[(c + 1) * ldu], xs[c + 1], s1);
+    // rows [r0, r0 + 64) above the block: thread (row rl, group g) takes the 16 columns g*16 ..
+    constexpr int kCols = kTrsvB / kTrsvGroups;
+    const int rl = tid % kTrsvRows, g = tid / kTrsvRows;
+    const long long r = (long long)blockIdx.x * kTrsvRows + rl;
+    double s = 0.0;
+    if (r < j0) {
+        const double* u = U + r + (j0 + g * kCols) * ldu;
+        double v[kCols];
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) v[c] = (g * kCols + c < b) ? u[c * ldu] : 0.0;
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) s = fma(v[c], xs[g * kCols + c], s);
     }
-    if (c < b) s0 = fma(u[c * ldu], xs[c], s0);
-    x[r] -= s0 + s1;
+    part[g][rl] = s;
+    __syncthreads();
+    if (g == 0 && r < j0) x[r] -= ((part[0][rl] + part[1][rl]) + (part[2][rl] + part[3][rl]));
 }
 
 // ---------------------------------------------------------------------------- GEMV
@@ -452,7 +460,7 @@ int dtrsv_unn(cudaStream_t st, int64_t n, const double* U, int64_t ldu, double* 
     for (int64_t j = nb - 1; j >= 0; --j) {
         const long long j0 = j * kTrsvB;
         const int b = (int)std::min<int64_t>(kTrsvB, n - j0);
-        const unsigned g = (unsigned)std::max<long long>(1, (j0 + kTrsvThreads - 1) / kTrsvThreads);
+        const unsigned g = (unsigned)std::max<long long>(1, (j0 + kTrsvRows - 1) / kTrsvRows);
         trsv_block_kernel<<<g, kTrsvThreads, 0, st>>>(U, (long long)ldu, x, work, j0, b);
         CHPL_CUDA(cudaGetLastError());
     }

@@ -78,6 +78,7 @@ SIGNATURES = {
     "chpl_panel_getrf_f64": (_int, [_vp, _i64, _i64, _vp, _sz, _vp, _vp, _vp]),
     "chpl_dgemm": (_int, [_vp, _i64, _i64, _i64, _dbl, _vp, _sz, _vp, _sz, _dbl, _vp, _sz]),
     "chpl_dtrsm_llnu": (_int, [_vp, _i64, _i64, _vp, _sz, _vp, _sz]),
+    "chpl_dtrtri_llnu": (_int, [_vp, _i64, _vp, _sz, _vp, _sz]),
     "chpl_dtrsv_unn": (_int, [_vp, _i64, _vp, _sz, _vp, _vp]),
     "chpl_dgemv": (_int, [_vp, _i64, _i64, _dbl, _vp, _sz, _vp, _dbl, _vp]),
     "chpl_residual": (_int, [_vp, _i64, _u64, _vp, _dp]),

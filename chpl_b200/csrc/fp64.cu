@@ -406,6 +406,29 @@ int trsm_rec(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_t 
     return trsm_rec(st, n - n1, nrhs, L + n1 + n1 * ldl, ldl, B + n1, ldb);
 }
 
+// X (n x n, ld ldx) = I: the starting point of the triangular inverse
+__global__ void set_identity_kernel(double* __restrict__ X, long long ldx, long long n)
+{
+    const long long total = n * n;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const long long i = e % n, j = e / n;
+        X[i + j * ldx] = (i == j) ? 1.0 : 0.0;
+    }
+}
+
+// X = inv(L) for X = I on entry: leaves solve L X = I in place; above them
+// X11 = inv(L11), X22 = inv(L22), X21 = -inv(L22) (L21 X11).  The zero upper
+// part is never touched.
+int trtri_rec(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx)
+{
+    if (n <= kLeaf) return trsm_rec(st, n, n, L, ldl, X, ldx);
+    const int64_t n1 = std::max<int64_t>(kLeaf, (n / 2) / kLeaf * kLeaf), n2 = n - n1;
+    CHPL_TRY(trtri_rec(st, n1, L, ldl, X, ldx));
+    CHPL_TRY(trtri_rec(st, n2, L + n1 + n1 * ldl, ldl, X + n1 + n1 * ldx, ldx));
+    CHPL_TRY(dgemm(st, n2, n1, n1, -1.0, L + n1, ldl, X, ldx, 0.0, X + n1, ldx));
+    return trsm_rec(st, n2, n1, L + n1 + n1 * ldl, ldl, X + n1, ldx);
+}
+
 int64_t trsm_count(int64_t n)
 {
     if (n <= kLeaf) return 1;
@@ -451,6 +474,27 @@ int dtrsm_llnu(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_
 
 int64_t dtrsm_launches(int64_t n) { return n <= 0 ? 0 : trsm_count(n); }
 
+int dtrtri_llnu(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx)
+{
+    if (n < 0 || ldl < std::max<int64_t>(n, 1) || ldx < std::max<int64_t>(n, 1)) {
+        set_error("dtrtri: bad sizes");
+        return CHPL_ERR_INVALID;
+    }
+    if (n == 0) return CHPL_OK;
+    const unsigned g = (unsigned)std::min<long long>((n * n + 255) / 256, 148LL * 32);
+    set_identity_kernel<<<g, 256, 0, st>>>(X, (long long)ldx, (long long)n);
+    CHPL_CUDA(cudaGetLastError());
+    return trtri_rec(st, n, L, ldl, X, ldx);
+}
+
+int64_t dtrtri_launches(int64_t n)
+{
+    if (n <= 0) return 0;
+    if (n <= kLeaf) return 1;
+    const int64_t n1 = std::max<int64_t>(kLeaf, (n / 2) / kLeaf * kLeaf);
+    return dtrtri_launches(n1) + dtrtri_launches(n - n1) + 1 + trsm_count(n - n1);
+}
+
 int dtrsv_unn(cudaStream_t st, int64_t n, const double* U, int64_t ldu, double* x, double* work)
 {
     if (n < 0 || ldu < std::max<int64_t>(n, 1)) { set_error("dtrsv: bad sizes"); return CHPL_ERR_INVALID; }
@@ -495,6 +539,11 @@ extern "C" int chpl_dgemm(void* stream, int64_t m, int64_t n, int64_t k, double 
 extern "C" int chpl_dtrsm_llnu(void* stream, int64_t n, int64_t nrhs, const double* L, size_t ldl, double* B, size_t ldb)
 {
     return dtrsm_llnu((cudaStream_t)stream, n, nrhs, L, (int64_t)ldl, B, (int64_t)ldb);
+}
+
+extern "C" int chpl_dtrtri_llnu(void* stream, int64_t n, const double* L, size_t ldl, double* X, size_t ldx)
+{
+    return dtrtri_llnu((cudaStream_t)stream, n, L, (int64_t)ldl, X, (int64_t)ldx);
 }
 
 extern "C" int chpl_dtrsv_unn(void* stream, int64_t n, const double* U, size_t ldu, double* x, double* work)

@@ -729,10 +729,8 @@ struct GridSolver {
         CHPL_NCCL(ncclBroadcast(piv, piv, (size_t)K, ncclInt64, root_of(ps, qs), g->world, st));
         if (pr == ps) {
             if (qc == qs) {
-                CHPL_TRY(identity(st, linv, K));
-                CHPL_TRY(dtrsm_llnu(st, K, K, A + lrb + lc * lda, lda, linv, K));
-                n_launch += dtrsm_launches(K);
-                ++n_launch;
+                CHPL_TRY(dtrtri_llnu(st, K, A + lrb + lc * lda, lda, linv, K));
+                n_launch += 1 + dtrtri_launches(K);
             }
             if (g->Q > 1) CHPL_NCCL(ncclBroadcast(linv, linv, (size_t)K * K, ncclDouble, qs, g->row, st));
         }
@@ -843,9 +841,8 @@ struct GridSolver {
         CHPL_CUDA(cudaEventRecord(e0, st));
         CHPL_TRY(factor_panel_p(A + J + lc * lda, lda, N - J, K, pv));
         CHPL_CUDA(cudaEventRecord(e1, st));
-        CHPL_TRY(identity(st, lv, K));
-        CHPL_TRY(dtrsm_llnu(st, K, K, A + J + lc * lda, lda, lv, K));
-        n_launch += dtrsm_launches(K);
+        CHPL_TRY(dtrtri_llnu(st, K, A + J + lc * lda, lda, lv, K));
+        n_launch += 1 + dtrtri_launches(K);
         const int64_t mW = N - J - K;
         if (mW > 0)
             CHPL_CUDA(cudaMemcpy2DAsync(arena, (size_t)mW * 8, A + J + K + lc * lda, (size_t)lda * 8, (size_t)mW * 8,
@@ -1081,9 +1078,8 @@ struct GridSolver {
                 CHPL_CUDA(cudaStreamWaitEvent(st, e2, 0));   // pk is free again
             }
             CHPL_CUDA(cudaEventRecord(evG, st));   // the W slots hold no panel any more
-            CHPL_TRY(identity(st, lv, K1));
-            CHPL_TRY(dtrsm_llnu(st, K1, K1, A + lrb1 + lc1 * lda, lda, lv, K1));
-            n_launch += dtrsm_launches(K1);
+            CHPL_TRY(dtrtri_llnu(st, K1, A + lrb1 + lc1 * lda, lda, lv, K1));
+            n_launch += 1 + dtrtri_launches(K1);
             if (mW1 > 0)
                 CHPL_CUDA(cudaMemcpy2DAsync(Wslot, (size_t)mW1 * 8, A + lrw1 + lc1 * lda, (size_t)lda * 8, (size_t)mW1 * 8,
                                             (size_t)K1, cudaMemcpyDeviceToDevice, st));

@@ -377,9 +377,8 @@ struct Solver {
         double* Li = Linv[s & 1];
         PhaseTimer::Rec r;
         CHPL_TRY(clk.begin(sP, PH_TRSM, r));
-        CHPL_TRY(identity(sP, Li, KJ));
-        CHPL_TRY(dtrsm_llnu(sP, KJ, KJ, at(J, J), ld, Li, KJ));
-        n_launch += 1 + dtrsm_launches(KJ);
+        CHPL_TRY(dtrtri_llnu(sP, KJ, at(J, J), ld, Li, KJ));
+        n_launch += 1 + dtrtri_launches(KJ);
         CHPL_TRY(clk.end(sP, r));
         const oz2::Moduli* M = oz2::moduli(cfg.moduli);
         const oz2::Layout y = oz2::layout((size_t)KJ, 256, (size_t)KJ, cfg.moduli, true, false);

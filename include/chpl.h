@@ -218,6 +218,11 @@ int chpl_dgemm(void *stream, int64_t m, int64_t n, int64_t k, double alpha, cons
  * read).  Replaces cublasDtrsm at src/chpl_single.cu:689-691, 708-710 and
  * src/chpl_p2.cu:1211-1220 (inv(L11) against the identity). */
 int chpl_dtrsm_llnu(void *stream, int64_t n, int64_t nrhs, const double *L, size_t ldl, double *B, size_t ldb);
+/* X (n x n) = L^-1 for L unit lower triangular: X's upper part is set to
+ * zero, its diagonal to one.  Recursive: X21 = -L22^-1 (L21 X11) on the DGEMM
+ * and TRSM above, 64-wide leaves.  Replaces the trsm of the identity with
+ * which the reference forms inv(L11) (src/chpl_p2.cu:1211-1220). */
+int chpl_dtrtri_llnu(void *stream, int64_t n, const double *L, size_t ldl, double *X, size_t ldx);
 /* x (n) = U^-1 x with U upper triangular, non-unit diagonal; work: n doubles
  * of device scratch.  Replaces cublasDtrsv at src/chpl_single.cu:724-725 (the
  * back solve, a one-column trsm there) and src/chpl_p2.cu:1851. */

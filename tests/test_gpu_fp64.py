@@ -122,6 +122,23 @@ def test_dtrsm_inverse_against_identity(cuda):
     assert np.array_equal(np.triu(Li, 1), np.zeros((n, n)))
 
 
+@pytest.mark.parametrize("n", [1, 64, 65, 200, 1024, 4096])
+def test_dtrtri_inverse(cuda, n):
+    """inv(L) by the structured recursion: L X = I to a few ulps times n, the
+    upper part exactly zero and the diagonal exactly one (X's prior contents
+    are overwritten)."""
+    L = _unit_lower(n, np.random.default_rng(n))
+    tL, pL, ldl = _buf(L)
+    tX, pX, ldx = _buf(np.full((n, n), np.nan), n + 3)
+    _lib.check(_lib.load().chpl_dtrtri_llnu(None, n, pL, ldl, pX, ldx), "chpl_dtrtri_llnu")
+    torch.cuda.synchronize()
+    X = _read(tX, n, n, ldx)
+    Lt = np.tril(L, -1) + np.eye(n)
+    assert np.array_equal(np.triu(X, 1), np.zeros((n, n))) and np.array_equal(np.diag(X), np.ones(n))
+    assert np.abs(Lt @ X - np.eye(n)).max() < 4 * n * U * np.abs(Lt).sum(axis=1).max() * np.abs(X).max()
+    assert np.allclose(X, np.linalg.inv(Lt), rtol=1e-9, atol=1e-12)
+
+
 @pytest.mark.parametrize("n", [1, 2, 63, 64, 65, 300, 2000, 9000])
 def test_dtrsv_matches_scipy(cuda, n):
     rng = np.random.default_rng(n)

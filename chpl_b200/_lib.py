@@ -68,6 +68,8 @@ SIGNATURES = {
     "chpl_oz2_split_tmp_bytes": (_sz, [_sz]),
     "chpl_oz2_products": (_int, [_vp, _sz, _sz, _sz, _uint, _vp, _sz, _vp, _sz, _sz, _vp, _sz]),
     "chpl_oz2_shift_bits": (_int, [_uint, _sz, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "chpl_oz1_worksize": (_int, [_sz, _sz, _sz, ctypes.POINTER(_sz)]),
+    "chpl_oz1_gemm": (_int, [_vp, _sz, _sz, _sz, _dbl, _vp, _sz, _vp, _sz, _dbl, _vp, _sz, _vp]),
     "chpl_matgen": (_int, [_vp, _vp, _sz, _sz, _sz, _i64, _i64, _i64, _u64]),
     "chpl_matgen_philox": (_int, [_vp, _vp, _sz, _sz, _sz, _i64, _i64, _i64, _u64]),
     "chpl_matgen_cyclic": (_int, [_vp, _vp, _sz, _i64, _i64, _int, _int, _int, _int, _u64]),

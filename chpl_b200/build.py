@@ -26,7 +26,7 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
                   "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
-LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "fp64.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu",
+LIB_SOURCES = ["capi.cu", "oz2.cu", "oz2_noalloc.cu", "oz1.cu", "fp64.cu", "hpl_kernels.cu", "panel.cu", "hpl_single.cu",
                "hpl_grid.cu", "diag.cu"]
 def _nccl_dir() -> str:
     """NCCL bundled with torch (the same library torch.distributed loads), so

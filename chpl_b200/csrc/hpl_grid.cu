@@ -1334,6 +1334,8 @@ static int grid_run(GridComm* g, const chpl_hpl_config* cfg, chpl_hpl_result* re
     if (cfg->P != g->P || cfg->Q != g->Q) { set_error("config grid %dx%d != communicator grid %dx%d", cfg->P, cfg->Q, g->P, g->Q); return CHPL_ERR_INVALID; }
     if (g->P > 2) { set_error("process grids with P > 2 are not supported (P = 1 or 2)"); return CHPL_ERR_UNSUPPORTED; }
     if (cfg->N <= 0 || cfg->NB <= 0 || cfg->NB > 16384) { set_error("bad N/NB"); return CHPL_ERR_INVALID; }
+    if (cfg->emulate < 0 || cfg->emulate > 2) { set_error("emulate must be 0, 1 or 2"); return CHPL_ERR_INVALID; }
+    if (cfg->emulate == 2) { set_error("the Ozaki-I update is the one-GPU engine's (chpl_hpl_run); the grid runs 0 or 1"); return CHPL_ERR_UNSUPPORTED; }
     GridSolver s;
     int rc = s.init(g, *cfg);
     auto finish = [&](int code) { s.destroy(); return code; };

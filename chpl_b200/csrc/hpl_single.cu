@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "fp64.h"
 #include "hpl.h"
+#include "oz1.h"
 #include "oz2.h"
 
 namespace chpl {
@@ -141,7 +142,7 @@ struct Solver {
         nsm = oz2::num_sms();
         reserve = cfg.lookahead ? (c.reserve_sms >= 0 ? c.reserve_sms : 16) : 0;
         reserve = std::min(reserve, nsm / 2);
-        emu_trsm = cfg.emulate && (cfg.trsm_mode == 1 || (cfg.trsm_mode == 0 && K > NB));
+        emu_trsm = cfg.emulate == 1 && (cfg.trsm_mode == 1 || (cfg.trsm_mode == 0 && K > NB));
         int lo = 0, hi = 0;
         CHPL_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
         CHPL_CUDA(cudaStreamCreateWithPriority(&s0, cudaStreamNonBlocking, lo));
@@ -153,9 +154,15 @@ struct Solver {
         const size_t bytesA = (size_t)ld * (size_t)ncols * sizeof(double);
         const int64_t mmax = std::max<int64_t>(N - NB, 0);
         const int64_t wide = std::max<int64_t>(ncols - K, 1);
-        chunk = cfg.chunk > 0 ? std::min<int64_t>(cfg.chunk, wide) : std::min<int64_t>(32768, wide);
-        size_t tot = 0, a_big = 0, b_big = 0, tot_in = 0, a_in = 0, b_in = 0;
-        if (cfg.emulate && mmax > 0) {
+        // Ozaki-I keeps kOz1Slices int32 products of m x chunk: 4096 columns by default
+        chunk = std::min<int64_t>(cfg.chunk > 0 ? cfg.chunk : (cfg.emulate == 2 ? 4096 : 32768), wide);
+        size_t tot = 0, a_big = 0, b_big = 0, tot_in = 0, a_in = 0, b_in = 0, oz1b = 0;
+        if (cfg.emulate == 2 && mmax > 0) {
+            if (chunk + 1024 > 65280) { set_error("ozaki-I: chunk must be <= 64256 columns"); return CHPL_ERR_INVALID; }
+            // every call has n <= chunk + 1023 (a narrow tail joins the last chunk) and k <= K
+            CHPL_TRY(chpl_oz1_worksize((size_t)mmax, (size_t)std::min<int64_t>(chunk + 1024, wide), (size_t)K, &oz1b));
+        }
+        if (cfg.emulate == 1 && mmax > 0) {
             const unsigned L = (unsigned)cfg.moduli;
             CHPL_TRY(chpl_oz2_worksize((size_t)mmax, (size_t)std::min<int64_t>(chunk + 1024, wide), (size_t)K, L, 1, 0,
                                        &tot, &a_big, &b_big));
@@ -167,7 +174,7 @@ struct Solver {
         size_t freeB = 0, totB = 0;
         CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
         const int npl = (int)((K + NB - 1) / NB);
-        const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0);
+        const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0) + oz1b * (cfg.lookahead ? 2 : 1);
         const size_t pbytes = panel_work_bytes(N, NB);
         const size_t need = bytesA + ozbytes + pbytes + 2 * npl * laswp_work_bytes(NB) + (size_t)(3 * N + 64) * 8 +
                             ((size_t)768 << 20);
@@ -204,6 +211,11 @@ struct Solver {
             }
             CHPL_CUDA(cudaMalloc(&w0, cfg.lookahead ? rest0 : std::max(rest0, restP)));
             if (cfg.lookahead) CHPL_CUDA(cudaMalloc(&wP, restP));
+            else wP = w0;
+        }
+        if (oz1b) {
+            CHPL_CUDA(cudaMalloc(&w0, oz1b));
+            if (cfg.lookahead) CHPL_CUDA(cudaMalloc(&wP, oz1b));
             else wP = w0;
         }
         return CHPL_OK;
@@ -265,6 +277,7 @@ struct Solver {
             CHPL_TRY(clk.end(st, r));
             return CHPL_OK;
         }
+        if (cfg.emulate == 2) return emu_oz1(st, work, mt, k, Am, lda_m, a0, c0, nc, Cp, alpha, beta);
         const oz2::Moduli* M = oz2::moduli(cfg.moduli);
         for (int64_t c = 0; c < nc;) {
             int64_t w = std::min(chunk, nc - c);
@@ -298,6 +311,30 @@ struct Solver {
             gemm_recs.push_back(g);
             ++n_launch;
             gemm_ops += 2.0 * (double)mt * (double)w * (double)y.kPad * cfg.moduli;
+            gemm_flops += 2.0 * (double)mt * (double)w * (double)k;
+            ++n_emu;
+            c += w;
+        }
+        return CHPL_OK;
+    }
+
+    // the same product through Ozaki scheme I (src/chpl_single.cu:617-630): digits, diagonal
+    // products and the reconstruction inside oz1::gemm, one call per column chunk
+    int emu_oz1(cudaStream_t st, void* work, int64_t mt, int64_t k, const double* Am, int64_t lda_m, int64_t a0,
+                int64_t c0, int64_t nc, double* Cp, double alpha, double beta)
+    {
+        for (int64_t c = 0; c < nc;) {
+            int64_t w = std::min(chunk, nc - c);
+            if (nc - c - w > 0 && nc - c - w < 1024) w = nc - c;
+            PhaseTimer::Rec g;
+            CHPL_TRY(clk.begin(st, PH_GEMM, g));
+            CHPL_TRY(oz1::gemm(st, (size_t)mt, (size_t)w, (size_t)k, alpha, Am, (size_t)lda_m, at(a0, c0 + c),
+                               (size_t)ld, beta, Cp + (size_t)c * ld, (size_t)ld, work));
+            CHPL_TRY(clk.end(st, g));
+            gemm_recs.push_back(g);
+            n_launch += oz1::launches();
+            const oz1::Layout y = oz1::layout((size_t)mt, (size_t)w, (size_t)k);
+            gemm_ops += 2.0 * (double)mt * (double)w * (double)y.ldk * oz1::kOz1Slices;
             gemm_flops += 2.0 * (double)mt * (double)w * (double)k;
             ++n_emu;
             c += w;
@@ -488,7 +525,8 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     if (cfg->agg < 0 || (int64_t)cfg->agg * cfg->NB > 16384) { set_error("agg * NB must be <= 16384"); return CHPL_ERR_INVALID; }
     if (cfg->P != 1 || cfg->Q != 1) { set_error("chpl_hpl_run drives one GPU; use the grid driver for P x Q > 1"); return CHPL_ERR_INVALID; }
     if (cfg->panel_mode != 0) { set_error("panel_mode: only this library's FP64 panel kernel (0) is built"); return CHPL_ERR_UNSUPPORTED; }
-    if (cfg->emulate && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
+    if (cfg->emulate < 0 || cfg->emulate > 2) { set_error("emulate must be 0 (FP64), 1 (Ozaki-II) or 2 (Ozaki-I)"); return CHPL_ERR_INVALID; }
+    if (cfg->emulate == 1 && !oz2::moduli(cfg->moduli)) { set_error("moduli must be in [2, 16]"); return CHPL_ERR_INVALID; }
     if (Ab && (int64_t)ldab < cfg->N) { set_error("ldab < N"); return CHPL_ERR_INVALID; }
     if (cfg->generator != CHPL_GEN_CHPL && cfg->generator != CHPL_GEN_PHILOX) {
         set_error("generator must be CHPL_GEN_CHPL or CHPL_GEN_PHILOX");

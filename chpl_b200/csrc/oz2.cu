@@ -296,6 +296,7 @@ struct GemmParams {
     int m, n;
     int mtiles, ntiles, kblocks;
     int rowsA, rowsB;   // padded rows per modulus plane in the residue buffers
+    int planeA;         // row offset between A's planes: rowsA, or 0 when every plane reads the same rows
     int mode;           // 0: CRT into C; 1: raw int32 products into P
     int group_m;
     double* C;
@@ -408,11 +409,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                             // the even CTA's full barrier counts both CTAs' bytes
                             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
                             const uint32_t fb = lead_full + stage * 8;
-                            tma_load_2d_pair(sa, &tmA, fb, kb * BK, l * p.rowsA + rowA);
+                            tma_load_2d_pair(sa, &tmA, fb, kb * BK, l * p.planeA + rowA);
                             tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * BK, l * p.rowsB + rowB);
                         } else {
                             mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                            tma_load_2d(sa, &tmA, &full[stage], kb * BK, l * p.rowsA + rowA);
+                            tma_load_2d(sa, &tmA, &full[stage], kb * BK, l * p.planeA + rowA);
                             tma_load_2d(sa + A_BYTES, &tmB, &full[stage], kb * BK, l * p.rowsB + rowB);
                         }
                         issued[stage] = (int)ph;
@@ -782,7 +783,8 @@ static int max_pair_clusters()
 
 int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsigned L, const int8_t* ra, size_t rowsA,
                 const int8_t* rb, size_t rowsB, const int32_t* shiftA, const int32_t* shiftB, double alpha,
-                double beta, double* C, size_t ldc, int32_t* P, size_t ldp, int8_t* scratch, int grid_max)
+                double beta, double* C, size_t ldc, int32_t* P, size_t ldp, int8_t* scratch, int grid_max,
+                long long planeA)
 {
     const Moduli* M = moduli((int)L);
     if (!M) { set_error("bad num_moduli"); return CHPL_ERR_INVALID; }
@@ -793,7 +795,9 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     if ((size_t)L * std::max(rowsA, rowsB) > 0x7fffffffull) { set_error("residue planes too tall"); return CHPL_ERR_UNSUPPORTED; }
     const bool pair = use_pair(m);
     CUtensorMap tmA, tmB;
-    CHPL_TRY(make_tmap_i8(&tmA, ra, kPad, (uint64_t)L * rowsA, BM));
+    if (planeA < 0) planeA = (long long)rowsA;
+    if (planeA != 0 && planeA != (long long)rowsA) { set_error("gemm_launch: A plane stride must be 0 or rowsA"); return CHPL_ERR_INVALID; }
+    CHPL_TRY(make_tmap_i8(&tmA, ra, kPad, (uint64_t)(L - 1) * (uint64_t)planeA + rowsA, BM));
     CHPL_TRY(make_tmap_i8(&tmB, rb, kPad, (uint64_t)L * rowsB, pair ? Form<true>::B_ROWS : BN));
     GemmParams p;
     std::memset(&p, 0, sizeof(p));
@@ -804,6 +808,7 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     p.ntiles = (int)((n + BN - 1) / BN);
     p.kblocks = (int)(kPad / BK);
     p.rowsA = (int)rowsA;
+    p.planeA = (int)planeA;
     p.rowsB = (int)rowsB;
     p.mode = mode;
     p.group_m = pair ? 8 : 16;

@@ -5,7 +5,7 @@ Configuration sources, as in the reference:
     N=16384, NB=1024, 16.0 when the file has fewer than 13 lines
     (src/chpl_p2.cu:570-584); lines 11/12 give P and Q.
   * chpl_single: ``HPLS_NB HPLS_AGG HPLS_BACKEND HPLS_SEED HPLS_G8_MODULI
-    HPLS_G8_FAST HPLS_G8_CHUNK`` (src/chpl_single.cu:842-869).
+    HPLS_G8_FAST HPLS_G8_CHUNK HPLS_OZ_NT`` (src/chpl_single.cu:842-869).
   * chpl_p2 / grid: ``CHPL2D_G8 CHPL2D_G8_MODULI CHPL2D_G8_FAST CHPL2D_G8_NT``
     (src/chpl_p2.cu:685-691) with the launcher defaults of
     scripts/mpirun_chpl:107-126 (G8=1, 11 moduli, fast).
@@ -81,7 +81,7 @@ class Config:
     P: int = 1
     Q: int = 1
     moduli: int = 11
-    emulate: bool = True
+    emulate: int = 1        # 0: FP64 update, 1: Ozaki-II, 2: Ozaki-I (one GPU only)
     fast: bool = True
     chunk: int = 0
     lookahead: bool = False
@@ -120,8 +120,9 @@ def single_config_from_env(N: int, env=None) -> Config:
     if gen not in ("philox", "chpl"):
         raise ValueError(f"unknown HPLS_GEN '{gen}'")
     c = Config(N=N, NB=_env_int(env, "HPLS_NB", 1024), moduli=_env_int(env, "HPLS_G8_MODULI", 11),
-               emulate=backend != "native", fast=bool(_env_int(env, "HPLS_G8_FAST", 1)),
-               chunk=_env_int(env, "HPLS_G8_CHUNK", 0), seed=_env_int(env, "HPLS_SEED", 42),
+               emulate={"native": 0, "gemmul8": 1, "ozaki": 2}[backend], fast=bool(_env_int(env, "HPLS_G8_FAST", 1)),
+               chunk=_env_int(env, "HPLS_OZ_NT" if backend == "ozaki" else "HPLS_G8_CHUNK", 0),
+               seed=_env_int(env, "HPLS_SEED", 42),
                lookahead=bool(_env_int(env, "HPLS_LOOKAHEAD", 0)), agg=_env_int(env, "HPLS_AGG", 0),
                generator=_lib.CHPL_GEN_PHILOX if gen == "philox" else _lib.CHPL_GEN_CHPL)
     if c.N <= 0 or c.NB <= 0 or c.NB > c.N:
@@ -255,7 +256,7 @@ def run_host(cfg: Config, Ab, ldab: int | None = None, verify: bool = True, want
 
 def format_single(res: Result, cfg: Config) -> str:
     """HPL-style report of chpl_single (src/chpl_single.cu:806-834)."""
-    tag = "HPLS_gemmul8" if cfg.emulate else "HPLS_native"
+    tag = "HPLS_" + ("native", "gemmul8", "ozaki")[int(cfg.emulate)]
     lines = ["=" * 58,
              "T/V                   N    NB   AGG      K           Time                 Gflops",
              "-" * 58,
@@ -267,7 +268,10 @@ def format_single(res: Result, cfg: Config) -> str:
     for p in PHASES:
         v = res.phases.get(p, 0.0)
         lines.append(f"{p:<14s}{v:9.3f}   {100.0 * v / max(res.time_s, 1e-30):6.2f}%")
-    lines.append(f"wide_gemm calls: gemmul8={res.n_emulated} (moduli={cfg.moduli} fast={int(cfg.fast)})")
+    if int(cfg.emulate) == 2:
+        lines.append(f"wide_gemm calls: ozaki={res.n_emulated} (slices=6)")
+    else:
+        lines.append(f"wide_gemm calls: gemmul8={res.n_emulated} (moduli={cfg.moduli} fast={int(cfg.fast)})")
     lines.append("=" * 58)
     return "\n".join(lines)
 

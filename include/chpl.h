@@ -148,6 +148,19 @@ int chpl_oz2_gemm_noalloc(void *stream, int opA, int opB, size_t m, size_t n, si
 /* scaling exponents (alpha, beta) used for num_moduli (host-only query) */
 int chpl_oz2_shift_bits(unsigned num_moduli, size_t k, int *alpha_bits, int *beta_bits);
 
+/*
+ * Ozaki scheme I emulated DGEMM, the reference's alternative engine
+ * (HPLS_BACKEND=ozaki; oz_gemm and its kernels, src/chpl_single.cu:147-236,
+ * 532-612): row / column power-of-two scales, six base-128 int8 digits per
+ * entry, the six anti-diagonals of digit products as int32 products on the
+ * tcgen05 int8 kernel, FP64 reconstruction.  C = alpha * A * B + beta * C,
+ * column-major, no transposes, k <= 21845, n <= 65280 per call; C may alias B
+ * when beta == 0.  `work` >= chpl_oz1_worksize bytes.
+ */
+int chpl_oz1_worksize(size_t m, size_t n, size_t k, size_t *work_bytes);
+int chpl_oz1_gemm(void *stream, size_t m, size_t n, size_t k, double alpha, const double *A, size_t lda,
+                  const double *B, size_t ldb, double beta, double *C, size_t ldc, void *work);
+
 /* ------------------------------------------------------------------------ */
 /* HPL building blocks                                                       */
 /* ------------------------------------------------------------------------ */
@@ -265,7 +278,8 @@ typedef struct chpl_hpl_config {
     int64_t NB;         /* panel width (HPL.dat line 8) */
     int P, Q;           /* process grid (rank = P*qc + pr) */
     int moduli;         /* CHPL2D_G8_MODULI / HPLS_G8_MODULI */
-    int emulate;        /* CHPL2D_G8 / HPLS_BACKEND=gemmul8: 1 = Ozaki-II update, 0 = FP64 */
+    int emulate;        /* CHPL2D_G8 / HPLS_BACKEND: 1 = Ozaki-II update (gemmul8), 0 = FP64 (native),
+                           2 = Ozaki-I (ozaki; one GPU only) */
     int fast;           /* CHPL2D_G8_FAST / HPLS_G8_FAST */
     int64_t chunk;      /* column chunk of the update (CHPL2D_G8_NT / HPLS_G8_CHUNK), 0 = auto */
     int lookahead;      /* depth-1 lookahead on a high-priority stream (1) or serial (0, default) */

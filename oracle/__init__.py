@@ -238,6 +238,55 @@ def hpl_residual_parts(y: np.ndarray, rs: np.ndarray, b: np.ndarray, x: np.ndarr
 
 
 # ---------------------------------------------------------------------------
+# Ozaki scheme I (the reference's alternative engine, HPLS_BACKEND=ozaki)
+# ---------------------------------------------------------------------------
+OZ1_SLICES = 6
+
+
+def _oz1_digits(x: np.ndarray) -> list[np.ndarray]:
+    """Base-128 digits of entries in (-1, 1): t = rint(128 x) clamped to 127,
+    x <- 128 x - t (ozsliceA/ozsliceB, src/chpl_single.cu:172-219).  The
+    digits are integers in [-128, 127] held as float64."""
+    out = []
+    x = x.copy()
+    for _ in range(OZ1_SLICES):
+        t = np.minimum(np.rint(x * 128.0), 127.0)
+        x = x * 128.0 - t
+        out.append(t)
+    return out
+
+
+def oz1_gemm(A: np.ndarray, B: np.ndarray, C: np.ndarray, alpha: float = -1.0, beta: float = 1.0) -> np.ndarray:
+    """C = alpha A B + beta C by Ozaki scheme I as the reference computes it
+    (src/chpl_single.cu:147-236, 532-612): power-of-two row / column scales
+    (ilogb(max) + 1), six base-128 digits, the anti-diagonals d = p + q < 6 of
+    the digit products in exact integers, reconstruction
+    sum_d P_d 128^-(d+2) in order d = 0..5, times 2^(ea_i + eb_j).  With
+    alpha = -1, beta = 1 (the solver's update) or beta = 0 the result is bit
+    for bit the GPU's (one rounding for alpha v + beta C either way)."""
+    A = np.asarray(A, np.float64)
+    B = np.asarray(B, np.float64)
+    ea = np.frexp(np.max(np.abs(A), axis=1))[1].astype(np.int64)
+    eb = np.frexp(np.max(np.abs(B), axis=0))[1].astype(np.int64)
+    da = _oz1_digits(np.ldexp(A, -ea[:, None]))
+    db = _oz1_digits(np.ldexp(B, -eb[None, :]))
+    acc = np.zeros((A.shape[0], B.shape[1]))
+    w = 2.0 ** -14
+    for d in range(OZ1_SLICES):
+        # every partial sum is an integer of magnitude < 6 k 2^14 < 2^53, so the
+        # float64 product is the exact integer whatever order BLAS sums in
+        P = np.hstack(da[:d + 1]) @ np.vstack(db[d::-1])
+        acc = acc + P * w
+        w *= 2.0 ** -7
+    v = np.ldexp(acc, (ea[:, None] + eb[None, :]))
+    if beta == 0.0:
+        return alpha * v
+    if alpha == -1.0 and beta == 1.0:
+        return C - v
+    return alpha * v + beta * C
+
+
+# ---------------------------------------------------------------------------
 # oracle/_ref: fragments of the reference's own source (oracle/ref_build.py)
 # ---------------------------------------------------------------------------
 _REF = os.path.join(_HERE, "_ref")

@@ -35,10 +35,16 @@ def test_single_usage():
     assert "usage: chpl_single N" in r.stderr
 
 
-@pytest.mark.parametrize("backend,msg", [("ozaki", "not part of this build"), ("bogus", "unknown HPLS_BACKEND")])
-def test_single_rejects_backend(backend, msg):
-    r = _run([SINGLE, "4096"], env={"HPLS_BACKEND": backend})
-    assert r.returncode == 1 and msg in r.stderr
+def test_single_rejects_backend():
+    r = _run([SINGLE, "4096"], env={"HPLS_BACKEND": "bogus"})
+    assert r.returncode == 1 and "unknown HPLS_BACKEND" in r.stderr
+
+
+def test_single_ozaki_backend_configuration():
+    """HPLS_BACKEND=ozaki selects the Ozaki-I update; HPLS_OZ_NT its column tile."""
+    r = _run([SINGLE, "8192"], env={"CHPL_DRY_RUN": "1", "HPLS_BACKEND": "ozaki", "HPLS_NB": "512", "HPLS_OZ_NT": "1024"})
+    assert r.returncode == 0, r.stderr
+    assert "backend=ozaki" in r.stdout and "chunk=1024" in r.stdout
 
 
 def test_single_rejects_bad_sizes():

@@ -43,7 +43,13 @@ def test_single_env_config():
            "HPLS_G8_CHUNK": "3072", "HPLS_SEED": "7"}
     c = hpl.single_config_from_env(8192, env)
     assert (c.N, c.NB, c.moduli, c.fast, c.chunk, c.seed, c.emulate) == (8192, 512, 12, True, 3072, 7, True)
-    assert hpl.single_config_from_env(2000, {"HPLS_BACKEND": "native"}).emulate is False
+    assert hpl.single_config_from_env(2000, {"HPLS_BACKEND": "native"}).emulate == 0
+    # HPLS_BACKEND=ozaki: the Ozaki-I update (emulate = 2), HPLS_OZ_NT columns per call
+    c = hpl.single_config_from_env(8192, {"HPLS_BACKEND": "ozaki", "HPLS_OZ_NT": "512", "HPLS_G8_CHUNK": "3072"})
+    assert (c.emulate, c.chunk, c.to_c().emulate) == (2, 512, 2)
+    assert hpl.format_single(hpl.Result(N=8192, NB=512, P=1, Q=1, time_s=1.0, tflops=1.0, resid=0.5, passed=True,
+                                        threshold=16.0, matgen_s=0.0),
+                             c).splitlines()[3].startswith("HPLS_ozaki")
     with pytest.raises(ValueError):
         hpl.single_config_from_env(2000, {"HPLS_BACKEND": "bogus"})
     with pytest.raises(ValueError):

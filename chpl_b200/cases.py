@@ -240,6 +240,8 @@ def main() -> None:
     h.add_argument("--reserve", type=int, default=-1)
     h.add_argument("--panel-mode", type=int, default=0)
     h.add_argument("--lookahead", action="store_true")
+    h.add_argument("--ozaki", action="store_true", help="the Ozaki-I update (emulate = 2)")
+    h.add_argument("--chunk", type=int, default=0)
     a = ap.parse_args()
     if a.what == "grid":
         grid_case(a.N, a.NB, a.moduli, a.grid)
@@ -255,10 +257,10 @@ def main() -> None:
         print(json.dumps(laswp_case(a.rows, a.cols, a.swaps, a.reps)), flush=True)
     else:
         r = hpl.run(hpl.Config(N=a.N, NB=a.NB, moduli=a.moduli, lookahead=a.lookahead and not a.no_lookahead,
-                               emulate=not a.fp64, agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve,
+                               emulate=0 if a.fp64 else 2 if a.ozaki else 1, chunk=a.chunk, agg=a.agg, trsm_mode=a.trsm_mode, reserve_sms=a.reserve,
                                panel_mode=a.panel_mode))
         print(json.dumps({"case": "hpl", "N": a.N, "NB": a.NB, "agg": a.agg, "trsm_mode": a.trsm_mode,
-                          "lookahead": a.lookahead, "panel_mode": a.panel_mode, "tflops": r.tflops, "time_s": r.time_s,
+                          "lookahead": a.lookahead, "reserve": a.reserve, "ozaki": a.ozaki, "tflops": r.tflops, "time_s": r.time_s,
                           "resid": r.resid, "passed": r.passed, "phases": r.phases,
                           "gemm_int8_tops": r.gemm_int8_ops / r.gemm_kernel_s / 1e12 if r.gemm_kernel_s else None,
                           "gemm_launches": r.gemm_launches}), flush=True)

@@ -32,9 +32,13 @@ int residual(cudaStream_t st, int64_t N, uint64_t seed, const double* x, double*
 int residual_matrix(cudaStream_t st, int64_t N, const double* Ab, size_t ld, const double* x, double* resid);
 int hpl_read_clear_status(int* st);
 size_t panel_work_bytes(int64_t m, int64_t n);
-// FP64 getrf of the m x n panel at A; ipiv[i] = base_row + pivot row within the panel
+// FP64 getrf of the m x n panel at A; ipiv[i] = base_row + pivot row within the panel.
+// max_ctas > 0 bounds the base kernel's cooperative grid (the SMs a concurrent
+// bulk update leaves free); 0 = one CTA per SM
 int panel_getrf(cudaStream_t st, int64_t m, int64_t n, double* A, size_t lda, int64_t* ipiv, int64_t base_row, int* info,
-                void* work);
+                void* work, int max_ctas = 0);
+// the fewest base-kernel CTAs that hold an m-row panel on chip (narrowest base block)
+int panel_min_ctas(int64_t m);
 int panel_status(void* work, int* err);
 
 }  // namespace chpl

@@ -141,6 +141,8 @@ struct Solver {
         ncols = N + 1;
         nsm = oz2::num_sms();
         reserve = cfg.lookahead ? (c.reserve_sms >= 0 ? c.reserve_sms : 16) : 0;
+        // the chain's panels must fit on the reserved SMs (4-column base blocks at the narrowest)
+        if (cfg.lookahead) reserve = std::max(reserve, panel_min_ctas(N));
         reserve = std::min(reserve, nsm / 2);
         emu_trsm = cfg.emulate == 1 && (cfg.trsm_mode == 1 || (cfg.trsm_mode == 0 && K > NB));
         int lo = 0, hi = 0;
@@ -380,7 +382,7 @@ struct Solver {
             void* plan = lw[s & 1][p];
             PhaseTimer::Rec r;
             CHPL_TRY(clk.begin(sP, PH_PANEL, r));
-            CHPL_TRY(panel_getrf(sP, N - jp, nb, at(jp, jp), (size_t)ld, ipiv + jp, jp, info + 1, pwork));
+            CHPL_TRY(panel_getrf(sP, N - jp, nb, at(jp, jp), (size_t)ld, ipiv + jp, jp, info + 1, pwork, cap));
             n_launch += 2 * ((nb + 15) / 16) * 2;
             CHPL_TRY(laswp_plan(sP, ipiv, jp, jp + nb, plan));
             n_launch += 2;

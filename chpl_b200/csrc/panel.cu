@@ -3,9 +3,11 @@
 // Replaces the cusolverDnXgetrf call of src/chpl_single.cu:668-679.
 // Recursive (left half, interchanges + U12 + Schur update, right half), down to
 // base blocks of at most 32 columns.  A base block is factored by one
-// cooperative kernel over up to all SMs: every CTA keeps a contiguous range of
-// the block's rows in shared memory, and the pivot of every column is found
-// with one exchange between the CTAs:
+// cooperative kernel over up to all SMs (or the SMs a concurrent update leaves
+// free: the base block then narrows to 16 / 8 / 4 columns until its rows fit
+// those CTAs): every CTA keeps a contiguous range of the block's rows in
+// shared memory, and the pivot of every column is found with one exchange
+// between the CTAs:
 //   * each CTA's candidate (largest |a| among its rows, smallest row on ties,
 //     as LAPACK's idamax) is published as one record: value, row, the
 //     candidate's whole row, and (CTA 0) the current diagonal row; then a
@@ -33,7 +35,8 @@
 
 namespace chpl {
 
-constexpr int kBaseW = 32;          // widest base block (16 / 8 when the rows do not fit on chip)
+constexpr int kBaseW = 32;          // widest base block (16 / 8 / 4 when the rows do not fit on chip)
+constexpr int kMinBaseW = 4;
 constexpr int kPanelThreads = 256;
 constexpr int kPanelWarps = kPanelThreads / 32;
 constexpr int kSmemBytes = 217600;  // shared memory of one base-kernel CTA (rows x width x 8 B)
@@ -291,6 +294,7 @@ static int handles(cudaStream_t st, PanelHandles** out)
         g_ph = PanelHandles();
         int nsm = 0, per = 0;
         CHPL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
@@ -322,6 +326,7 @@ struct PanelCtx {
     PanelRec* recs;
     void* plan;
     unsigned int sbase;  // barrier arrivals so far in this call
+    int cap;             // CTAs of a base kernel at most
     int* info;
     int* status;
 };
@@ -331,7 +336,7 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
     // the fewest CTAs whose shared memory holds the block (fewer flags to
     // exchange per column), at most one per SM, at least 4 rows per thread-pass
     const int64_t rows_fit = kSmemBytes / ((int64_t)w * (int64_t)sizeof(double));
-    const int G = (int)std::max<int64_t>(1, std::min<int64_t>(c.h->grid, (m + rows_fit - 1) / rows_fit));
+    const int G = (int)std::max<int64_t>(1, std::min<int64_t>(c.cap, (m + rows_fit - 1) / rows_fit));
     const int64_t rows_per = (m + G - 1) / G;
     const size_t smem = (size_t)rows_per * w * sizeof(double);
     if (G > kPanelThreads - kBaseW) {   // the record fetchers and the diagonal-row fetchers must not overlap
@@ -344,8 +349,10 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
     }
     long long ldl = (long long)lda, ml = (long long)m, rp = (long long)rows_per, br = (long long)base_row;
     void* args[] = {&A, &ldl, &ml, &w, &rp, &ipiv, &br, &c.info, &info_off, &c.sync, &c.flags, &c.sbase, &c.recs};
-    const void* fn = w <= 8 ? (const void*)panel_base_kernel<8>
-                   : w <= 16 ? (const void*)panel_base_kernel<16> : (const void*)panel_base_kernel<32>;
+    const void* fn = w <= 4    ? (const void*)panel_base_kernel<4>
+                   : w <= 8  ? (const void*)panel_base_kernel<8>
+                   : w <= 16 ? (const void*)panel_base_kernel<16>
+                             : (const void*)panel_base_kernel<32>;
     CHPL_CUDA(cudaLaunchCooperativeKernel(fn, dim3(G), dim3(kPanelThreads), args, smem, c.st));
     c.sbase += (unsigned int)w;
     return CHPL_OK;
@@ -354,9 +361,14 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
 // ipiv entries of this node are relative to the node's top row + base_row
 int rec(PanelCtx& c, double* A, int64_t lda, int64_t m, int64_t n, int64_t* ipiv, int64_t base_row, int info_off)
 {
-    // base width: the widest of 32 / 16 / 8 columns whose rows fit on chip
-    const int64_t rows_sm = (m + c.h->grid - 1) / c.h->grid;
-    const int bw = rows_sm * 32 * 8 <= kSmemBytes ? 32 : rows_sm * 16 * 8 <= kSmemBytes ? 16 : 8;
+    // base width: the widest of 32 / 16 / 8 / 4 columns whose rows fit in the CTAs allowed
+    const int64_t rows_sm = (m + c.cap - 1) / c.cap;
+    int bw = kBaseW;
+    while (bw > kMinBaseW && rows_sm * bw * (int64_t)sizeof(double) > kSmemBytes) bw /= 2;
+    if (rows_sm * bw * (int64_t)sizeof(double) > kSmemBytes) {
+        set_error("panel of %lld rows does not fit in the shared memory of %d CTAs", (long long)m, c.cap);
+        return CHPL_ERR_UNSUPPORTED;
+    }
     if (n <= bw) return base_block(c, A, lda, m, (int)n, ipiv, base_row, info_off);
     int64_t n1 = ((n / 2) + bw - 1) / bw * bw;
     const int64_t n2 = n - n1;
@@ -379,8 +391,14 @@ int rec(PanelCtx& c, double* A, int64_t lda, int64_t m, int64_t n, int64_t* ipiv
 }  // namespace
 
 // Factor the m x n panel at A; ipiv[i] = base_row + (0-based pivot row within the panel).
+int panel_min_ctas(int64_t m)
+{
+    const int64_t rows_fit = kSmemBytes / (kMinBaseW * (int64_t)sizeof(double));
+    return (int)std::max<int64_t>(1, (m + rows_fit - 1) / rows_fit);
+}
+
 int panel_getrf(cudaStream_t st, int64_t m, int64_t n, double* A, size_t lda, int64_t* ipiv, int64_t base_row, int* info,
-                void* work)
+                void* work, int max_ctas)
 {
     if (m < n || n <= 0 || (int64_t)lda < m) { set_error("panel_getrf: need m >= n > 0, lda >= m"); return CHPL_ERR_INVALID; }
     PanelHandles* h = nullptr;
@@ -397,6 +415,7 @@ int panel_getrf(cudaStream_t st, int64_t m, int64_t n, double* A, size_t lda, in
     w += round_up(2 * kMaxPanelCTAs * sizeof(PanelRec), 256);
     c.plan = w;
     c.sbase = 0;
+    c.cap = max_ctas > 0 ? std::min(max_ctas, h->grid) : h->grid;
     c.info = info;
     CHPL_CUDA(cudaMemsetAsync(c.sync, 0, round_up(sizeof(PanelSync), 256) + kMaxPanelCTAs * sizeof(unsigned int), st));
     return rec(c, A, (int64_t)lda, m, n, ipiv, base_row, 0);

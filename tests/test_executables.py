@@ -104,6 +104,18 @@ def test_single_gemmtest(cuda):
 
 
 @pytest.mark.gpu
+def test_single_ozaki_gemmtest_and_solve(cuda):
+    """HPLS_BACKEND=ozaki: the reference's gemmtest form (n in tiles of nt
+    columns) and a whole solve through the Ozaki-I update."""
+    r = _run([SINGLE, "--gemmtest", "1500", "1024", "900", "256"], env={"HPLS_BACKEND": "ozaki"})
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "GEMMTEST_PASS" in r.stdout and "(ozaki)" in r.stdout
+    r = _run([SINGLE, "8192"], env={"HPLS_BACKEND": "ozaki", "HPLS_NB": "512", "HPLS_AGG": "4", "HPLS_OZ_NT": "512"})
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "HPLS_ozaki" in r.stdout and "PASSED" in r.stdout and "wide_gemm calls: ozaki=" in r.stdout
+
+
+@pytest.mark.gpu
 def test_p2_one_rank(cuda, tmp_path):
     dat = tmp_path / "HPL.dat"
     _dat(dat, 5000, 512)

@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle
-from chpl_b200 import hpl
+from chpl_b200 import _lib, hpl
 
 pytestmark = pytest.mark.gpu
 
@@ -79,6 +79,9 @@ def test_grid_1x1_fp64_update(cuda):
         dist.init_process_group("gloo", rank=0, world_size=1)
     g = grid.Grid(1, 1)
     r = g.run(hpl.Config(N=3000, NB=512, P=1, Q=1, emulate=False), want_x=True)
+    # the Ozaki-I update is the one-GPU engine's only: an error, and the grid stays usable
+    with pytest.raises(_lib.ChplError, match="Ozaki-I"):
+        g.run(hpl.Config(N=2048, NB=256, P=1, Q=1, emulate=2))
     g.close()
     assert r.passed and r.resid < 1.0, r.resid
     # forward error of two backward-stable solves of a system with condition ~1e5

@@ -148,6 +148,15 @@ def test_hpl_emulated_passes(cuda, L):
     assert res.n_emulated > 0
 
 
+@pytest.mark.parametrize("lookahead", [False, True])
+def test_hpl_ozaki1_passes(cuda, lookahead):
+    """emulate = 2: every trailing update through Ozaki scheme I (six
+    base-128 digits), column chunks of 1536 with a narrow tail joined."""
+    res = hpl.run(hpl.Config(N=6000, NB=256, emulate=2, chunk=1536, lookahead=lookahead), want_x=True)
+    assert res.passed, res.resid
+    assert res.n_emulated > 0
+
+
 def test_hpl_config1_passes_at_11_moduli(cuda):
     """The chpl_p2 fallback size (N = 16384, NB = 1024, 11 moduli) with the library's
     default aggregation passes the HPL check with margin (the aggregated

@@ -26,6 +26,7 @@
 // (fp64.cu); interchanges use the device-built net permutation of
 // hpl_kernels.cu.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -37,8 +38,6 @@ namespace chpl {
 
 constexpr int kBaseW = 32;          // widest base block (16 / 8 / 4 when the rows do not fit on chip)
 constexpr int kMinBaseW = 4;
-constexpr int kPanelThreads = 256;
-constexpr int kPanelWarps = kPanelThreads / 32;
 constexpr int kSmemBytes = 217600;  // shared memory of one base-kernel CTA (rows x width x 8 B)
 constexpr int kMaxPanelCTAs = 1024;
 
@@ -75,8 +74,8 @@ __device__ __forceinline__ bool better(double v, long long r, double bv, long lo
 // Factor the m x w block at A (ld) in place, w <= W.  ipiv[j] = base_row +
 // pivot row (block-relative).  info: 1-based column of the first exact zero
 // pivot (+ info_off), left unchanged otherwise.
-template <int W>
-__global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __restrict__ A, long long ld, long long m,
+template <int W, int T>
+__global__ void __launch_bounds__(T) panel_base_kernel(double* __restrict__ A, long long ld, long long m,
                                                                     int w, long long rows_per, int64_t* __restrict__ ipiv,
                                                                     long long base_row, int* __restrict__ info,
                                                                     int info_off, PanelSync* sync, unsigned int* flags,
@@ -84,6 +83,7 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
 {
     extern __shared__ double S[];  // column-major [W][rows_per]: conflict-free row-parallel access
     __shared__ double pv[W], tv[W];
+    constexpr int kPanelWarps = T / 32;
     __shared__ double stage[kPanelWarps][W], stage_top[W];
     __shared__ double wv[kPanelWarps];
     __shared__ long long wr[kPanelWarps];
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
         };
         // threads [0, G) fetch the CTAs' records, threads [kTopT, kTopT + w) the diagonal
         // row from CTA 0's record, both at once
-        constexpr int kTopT = kPanelThreads - W;
+        constexpr int kTopT = T - W;
         if (tid < G) {
             good = poll(tid) ? 1 : 0;
             if (good) {  // the whole record in one round trip
@@ -282,7 +282,23 @@ __global__ void __launch_bounds__(kPanelThreads) panel_base_kernel(double* __res
 struct PanelHandles {
     int dev = -1;
     int grid = 0;
+    int threads = 256;
+    int min_rows = 0;
 };
+
+// the base kernel for block width w (<= 4, 8, 16, 32) and t threads (256 or 512)
+static const void* base_kernel(int w, int t)
+{
+    if (t == 512)
+        return w <= 4    ? (const void*)panel_base_kernel<4, 512>
+               : w <= 8  ? (const void*)panel_base_kernel<8, 512>
+               : w <= 16 ? (const void*)panel_base_kernel<16, 512>
+                         : (const void*)panel_base_kernel<32, 512>;
+    return w <= 4    ? (const void*)panel_base_kernel<4, 256>
+           : w <= 8  ? (const void*)panel_base_kernel<8, 256>
+           : w <= 16 ? (const void*)panel_base_kernel<16, 256>
+                     : (const void*)panel_base_kernel<32, 256>;
+}
 
 static thread_local PanelHandles g_ph;
 
@@ -294,15 +310,25 @@ static int handles(cudaStream_t st, PanelHandles** out)
         g_ph = PanelHandles();
         int nsm = 0, per = 0;
         CHPL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        CHPL_CUDA(cudaFuncSetAttribute(panel_base_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        CHPL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, panel_base_kernel<32>, kPanelThreads, kSmemBytes));
-        if (per < 1) { set_error("panel kernel does not fit on an SM"); return CHPL_ERR_UNSUPPORTED; }
+        for (int t = 0; t < 2; ++t)
+            for (int wi = 0; wi < 4; ++wi) {
+                CHPL_CUDA(cudaFuncSetAttribute(base_kernel(4 << wi, 256 << t), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kSmemBytes));
+                CHPL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, base_kernel(4 << wi, 256 << t), 256 << t,
+                                                                        kSmemBytes));
+                if (per < 1) { set_error("panel kernel does not fit on an SM"); return CHPL_ERR_UNSUPPORTED; }
+            }
         g_ph.grid = nsm;  // one CTA per SM: co-resident by construction
         g_ph.dev = dev;
     }
+    // tuning, read at every call: CTA size (CHPL_PANEL_THREADS 256 | 512) and the rows
+    // a CTA is given at least (CHPL_PANEL_ROWS; 0: the fewest CTAs that hold the block).
+    // Every element receives the same operations in the same order either way.
+    const char* e = std::getenv("CHPL_PANEL_THREADS");
+    g_ph.threads = (e && std::atoi(e) == 512) ? 512 : 256;
+    e = std::getenv("CHPL_PANEL_ROWS");
+    g_ph.min_rows = e ? std::max(0, std::atoi(e)) : 0;
+    if (g_ph.min_rows > 0) g_ph.min_rows = std::max(g_ph.min_rows, 64);
     (void)st;
     *out = &g_ph;
     return CHPL_OK;
@@ -334,13 +360,19 @@ struct PanelCtx {
 int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* ipiv, int64_t base_row, int info_off)
 {
     // the fewest CTAs whose shared memory holds the block (fewer flags to
-    // exchange per column), at most one per SM, at least 4 rows per thread-pass
+    // exchange per column), or more when min_rows asks for smaller row ranges,
+    // at most one per SM
     const int64_t rows_fit = kSmemBytes / ((int64_t)w * (int64_t)sizeof(double));
-    const int G = (int)std::max<int64_t>(1, std::min<int64_t>(c.cap, (m + rows_fit - 1) / rows_fit));
+    int64_t want = (m + rows_fit - 1) / rows_fit;
+    if (c.h->min_rows > 0) want = std::max<int64_t>(want, m / c.h->min_rows);
+    // CTA 0 holds the block's top w rows (the diagonal rows the kernel reads from it)
+    want = std::min<int64_t>(want, std::max<int64_t>(1, m / w));
+    const int G = (int)std::max<int64_t>(1, std::min<int64_t>(c.cap, want));
     const int64_t rows_per = (m + G - 1) / G;
     const size_t smem = (size_t)rows_per * w * sizeof(double);
-    if (G > kPanelThreads - kBaseW) {   // the record fetchers and the diagonal-row fetchers must not overlap
-        set_error("panel: %d CTAs exceed the exchange's %d record threads", G, kPanelThreads - kBaseW);
+    const int T = c.h->threads;
+    if (G > T - kBaseW) {   // the record fetchers and the diagonal-row fetchers must not overlap
+        set_error("panel: %d CTAs exceed the exchange's %d record threads", G, T - kBaseW);
         return CHPL_ERR_UNSUPPORTED;
     }
     if (smem > (size_t)kSmemBytes) {
@@ -349,11 +381,7 @@ int base_block(PanelCtx& c, double* A, int64_t lda, int64_t m, int w, int64_t* i
     }
     long long ldl = (long long)lda, ml = (long long)m, rp = (long long)rows_per, br = (long long)base_row;
     void* args[] = {&A, &ldl, &ml, &w, &rp, &ipiv, &br, &c.info, &info_off, &c.sync, &c.flags, &c.sbase, &c.recs};
-    const void* fn = w <= 4    ? (const void*)panel_base_kernel<4>
-                   : w <= 8  ? (const void*)panel_base_kernel<8>
-                   : w <= 16 ? (const void*)panel_base_kernel<16>
-                             : (const void*)panel_base_kernel<32>;
-    CHPL_CUDA(cudaLaunchCooperativeKernel(fn, dim3(G), dim3(kPanelThreads), args, smem, c.st));
+    CHPL_CUDA(cudaLaunchCooperativeKernel(base_kernel(w, T), dim3(G), dim3(T), args, smem, c.st));
     c.sbase += (unsigned int)w;
     return CHPL_OK;
 }

@@ -91,6 +91,31 @@ def test_panel_getrf(cuda, mn):
     assert np.allclose(got, lu, rtol=1e-11, atol=1e-12)
 
 
+@pytest.mark.parametrize("m,n", [(139264, 40), (20000, 70)])
+def test_panel_getrf_launch_shapes_agree(cuda, m, n, monkeypatch):
+    """CTA size (256 / 512 threads) and rows per CTA change only the launch:
+    every element gets the same operations in the same order, so the factors
+    and pivots are bit-identical, and the pivots are LAPACK's."""
+    L = _lib.load()
+    A = np.random.default_rng(m).uniform(-0.5, 0.5, (m, n))
+    outs = []
+    for threads, rows in (("256", "0"), ("512", "0"), ("256", "300"), ("512", "1000")):
+        monkeypatch.setenv("CHPL_PANEL_THREADS", threads)
+        monkeypatch.setenv("CHPL_PANEL_ROWS", rows)
+        dA, lda = to_dev(A)
+        piv = torch.zeros(n, dtype=torch.int64, device="cuda")
+        info = torch.zeros(1, dtype=torch.int32, device="cuda")
+        work = empty_bytes(L.chpl_panel_getrf_work_bytes(m, n))
+        _lib.check(L.chpl_panel_getrf_f64(0, m, n, dA.data_ptr(), lda, piv.data_ptr(), info.data_ptr(),
+                                          work.data_ptr()), "panel_getrf")
+        torch.cuda.synchronize()
+        outs.append((from_dev(dA, m, n), piv.cpu().numpy()))
+    for lu, p in outs[1:]:
+        assert np.array_equal(lu.view(np.uint64), outs[0][0].view(np.uint64))
+        assert np.array_equal(p, outs[0][1])
+    assert np.array_equal(outs[0][1], scipy.linalg.lu_factor(A)[1])
+
+
 def test_panel_getrf_zero_pivot(cuda):
     """An exactly singular panel reports the first zero pivot (LAPACK info) without faulting."""
     L = _lib.load()

@@ -65,6 +65,7 @@ struct GemmArgs {
     long long ldb;
     double* C;
     long long ldc;
+    long long sA, sB, sC;   // batch strides (doubles) between the products of a batched launch
     int vecA, vecB;      // 16-byte copies allowed for A / B
 };
 
@@ -96,6 +97,9 @@ __global__ void __launch_bounds__(WM * WN * 32, MINB) dgemm_kernel(GemmArgs p)
     const int wm0 = (warp % WM) * (BM / WM), wn0 = (warp / WM) * (BN / WN);
     const long long m0 = (long long)blockIdx.x * BM, n0 = (long long)blockIdx.y * BN;
     const long long ktiles = (p.k + kBK - 1) / kBK;
+    const double* Ag = p.A + blockIdx.z * p.sA;   // this CTA's product of a batch
+    const double* Bg = p.B + blockIdx.z * p.sB;
+    double* Cg = p.C + blockIdx.z * p.sC;
 
     auto load_tile = [&](int stage, long long kt) {
         const long long k0 = kt * kBK;
@@ -107,14 +111,14 @@ __global__ void __launch_bounds__(WM * WN * 32, MINB) dgemm_kernel(GemmArgs p)
                 const long long gr = m0 + r, gk = k0 + kk;
                 const long long left = (gk < p.k) ? p.m - gr : 0;
                 const int nb = left >= 2 ? 16 : (left == 1 ? 8 : 0);
-                cp_async(as + kk * S::kPA + r, nb ? p.A + gr + gk * p.lda : p.A, 16, nb);
+                cp_async(as + kk * S::kPA + r, nb ? Ag + gr + gk * p.lda : Ag, 16, nb);
             }
         } else {
             for (int e = tid; e < kBK * BM; e += S::kThreads) {
                 const int kk = e / BM, r = e % BM;
                 const long long gr = m0 + r, gk = k0 + kk;
                 const bool ok = gk < p.k && gr < p.m;
-                cp_async(as + kk * S::kPA + r, ok ? p.A + gr + gk * p.lda : p.A, 8, ok ? 8 : 0);
+                cp_async(as + kk * S::kPA + r, ok ? Ag + gr + gk * p.lda : Ag, 8, ok ? 8 : 0);
             }
         }
         if (p.vecB) {
@@ -123,14 +127,14 @@ __global__ void __launch_bounds__(WM * WN * 32, MINB) dgemm_kernel(GemmArgs p)
                 const long long gc = n0 + c, gk = k0 + kk;
                 const long long left = (gc < p.n) ? p.k - gk : 0;
                 const int nb = left >= 2 ? 16 : (left == 1 ? 8 : 0);
-                cp_async(bs + c * kPB + kk, nb ? p.B + gk + gc * p.ldb : p.B, 16, nb);
+                cp_async(bs + c * kPB + kk, nb ? Bg + gk + gc * p.ldb : Bg, 16, nb);
             }
         } else {
             for (int e = tid; e < BN * kBK; e += S::kThreads) {
                 const int c = e / kBK, kk = e % kBK;
                 const long long gc = n0 + c, gk = k0 + kk;
                 const bool ok = gc < p.n && gk < p.k;
-                cp_async(bs + c * kPB + kk, ok ? p.B + gk + gc * p.ldb : p.B, 8, ok ? 8 : 0);
+                cp_async(bs + c * kPB + kk, ok ? Bg + gk + gc * p.ldb : Bg, 8, ok ? 8 : 0);
             }
         }
     };
@@ -190,14 +194,14 @@ __global__ void __launch_bounds__(WM * WN * 32, MINB) dgemm_kernel(GemmArgs p)
                 const long long r = m0 + wm0 + i * 16 + gid + (q >= 2 ? 8 : 0);
                 const long long c = n0 + wn0 + j * 8 + tig * 2 + (q & 1);
                 if (r < p.m && c < p.n) {
-                    double* cp = p.C + r + c * p.ldc;
+                    double* cp = Cg + r + c * p.ldc;
                     *cp = p.beta == 0.0 ? p.alpha * acc[i][j][q] : fma(p.alpha, acc[i][j][q], p.beta * *cp);
                 }
             }
 }
 
 template <int BM, int BN, int WM, int WN, int MINB>
-int launch_gemm(cudaStream_t st, const GemmArgs& a)
+int launch_gemm(cudaStream_t st, const GemmArgs& a, int batch)
 {
     using S = GemmShape<BM, BN, WM, WN, MINB>;
     static bool attr_done[64] = {};
@@ -210,7 +214,7 @@ int launch_gemm(cudaStream_t st, const GemmArgs& a)
     }
     const long long tm = (a.m + BM - 1) / BM, tn = (a.n + BN - 1) / BN;
     if (tm > 0x7fffffffLL || tn > 65535) { set_error("dgemm: %lld x %lld tiles exceed the grid", tm, tn); return CHPL_ERR_UNSUPPORTED; }
-    dgemm_kernel<BM, BN, WM, WN, MINB><<<dim3((unsigned)tm, (unsigned)tn), S::kThreads, S::kSmem, st>>>(a);
+    dgemm_kernel<BM, BN, WM, WN, MINB><<<dim3((unsigned)tm, (unsigned)tn, (unsigned)batch), S::kThreads, S::kSmem, st>>>(a);
     CHPL_CUDA(cudaGetLastError());
     return CHPL_OK;
 }
@@ -266,8 +270,11 @@ constexpr int kLeafWarps = 8;
 
 __global__ void __launch_bounds__(kLeafWarps * 32) trsm_leaf_warp_kernel(int n, const double* __restrict__ L,
                                                                         long long ldl, double* __restrict__ B,
-                                                                        long long ldb, long long nrhs)
+                                                                        long long ldb, long long nrhs, long long bsL,
+                                                                        long long bsB)
 {
+    L += blockIdx.y * bsL;   // one independent solve per blockIdx.y (batch strides bsL, bsB)
+    B += blockIdx.y * bsB;
     __shared__ double Ls[kLeaf][kLeaf + 1];   // Ls[j][i] = L(i, j)
     for (int e = threadIdx.x; e < kLeaf * kLeaf; e += blockDim.x) {
         const int i = e % kLeaf, j = e / kLeaf;
@@ -389,7 +396,7 @@ int trsm_rec(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_t 
         if (nrhs < 32768) {   // few right-hand sides: a warp each
             const long long g = (nrhs + kLeafWarps - 1) / kLeafWarps;
             trsm_leaf_warp_kernel<<<(unsigned)g, kLeafWarps * 32, 0, st>>>((int)n, L, (long long)ldl, B, (long long)ldb,
-                                                                           (long long)nrhs);
+                                                                           (long long)nrhs, 0LL, 0LL);
         } else {
             const long long g = (nrhs + kLeafThreads - 1) / kLeafThreads;
             if (g > 0x7fffffffLL) { set_error("dtrsm: too many right-hand sides"); return CHPL_ERR_UNSUPPORTED; }
@@ -416,14 +423,79 @@ __global__ void set_identity_kernel(double* __restrict__ X, long long ldx, long 
     }
 }
 
-// X = inv(L) for X = I on entry: leaves solve L X = I in place; above them
-// X11 = inv(L11), X22 = inv(L22), X21 = -inv(L22) (L21 X11).  The zero upper
-// part is never touched.
+// C_z = alpha A_z B_z + beta C_z for z < batch, with A_z = A + z * sA (doubles) and
+// likewise B_z, C_z: every product m x n x k, one launch (blockIdx.z = z)
+int gemm_batched(cudaStream_t st, int64_t m, int64_t n, int64_t k, double alpha, const double* A, int64_t lda,
+                 int64_t sA, const double* B, int64_t ldb, int64_t sB, double beta, double* C, int64_t ldc, int64_t sC,
+                 int64_t batch)
+{
+    if (batch > 65535) { set_error("dgemm: batch of %lld exceeds the grid", (long long)batch); return CHPL_ERR_UNSUPPORTED; }
+    GemmArgs a;
+    a.m = m; a.n = n; a.k = k; a.alpha = alpha; a.beta = beta;
+    a.A = A; a.lda = lda; a.B = B; a.ldb = ldb; a.C = C; a.ldc = ldc;
+    a.sA = sA; a.sB = sB; a.sC = sC;
+    a.vecA = ((reinterpret_cast<uintptr_t>(A) & 15) == 0 && (lda & 1) == 0 && (sA & 1) == 0) ? 1 : 0;
+    a.vecB = ((reinterpret_cast<uintptr_t>(B) & 15) == 0 && (ldb & 1) == 0 && (sB & 1) == 0) ? 1 : 0;
+    if (m <= 64) return launch_gemm<64, 128, 2, 4, 2>(st, a, (int)batch);
+    if (n <= 32) return launch_gemm<128, 32, 4, 1, 2>(st, a, (int)batch);
+    return launch_gemm<128, 64, 4, 2, 2>(st, a, (int)batch);
+}
+
+// zero the b x b blocks X + z * stride, z < nblk
+__global__ void zero_blocks_kernel(double* __restrict__ X, long long ldx, long long b, long long stride, long long nblk)
+{
+    const long long per = b * b, total = per * nblk;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+        const long long z = e / per, r = e % per;
+        X[z * stride + (r % b) + (r / b) * ldx] = 0.0;
+    }
+}
+
+bool leaves_pow2(int64_t n)
+{
+    if (n < kLeaf || n % kLeaf) return false;
+    const int64_t q = n / kLeaf;
+    return (q & (q - 1)) == 0;
+}
+
+// X = inv(L) for n = kLeaf * 2^q and X = I on entry, level by level with every
+// pair of a level in one launch: the diagonal leaves (L_b X_b = I, batched),
+// then for b = kLeaf, 2 kLeaf, .. < n and all pairs of b-blocks at once
+//   U = L21 X11       (into the pair's block above the diagonal, which is zero)
+//   X21 = -X22 U      (= -inv(L22) L21 inv(L11))
+//   U = 0
+// 1 + 3 log2(n / kLeaf) launches.
+int trtri_pow2(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx)
+{
+    const int64_t nl = n / kLeaf;
+    if (nl > 65535) { set_error("dtrtri: %lld leaves exceed the grid", (long long)nl); return CHPL_ERR_UNSUPPORTED; }
+    trsm_leaf_warp_kernel<<<dim3(kLeaf / kLeafWarps, (unsigned)nl), kLeafWarps * 32, 0, st>>>(
+        kLeaf, L, (long long)ldl, X, (long long)ldx, (long long)kLeaf, (long long)kLeaf * (1 + ldl),
+        (long long)kLeaf * (1 + ldx));
+    CHPL_CUDA(cudaGetLastError());
+    for (int64_t b = kLeaf; b < n; b *= 2) {
+        const int64_t np = n / (2 * b), sL = 2 * b * (1 + ldl), sX = 2 * b * (1 + ldx);
+        CHPL_TRY(gemm_batched(st, b, b, b, 1.0, L + b, ldl, sL, X, ldx, sX, 0.0, X + b * ldx, ldx, sX, np));
+        CHPL_TRY(gemm_batched(st, b, b, b, -1.0, X + b + b * ldx, ldx, sX, X + b * ldx, ldx, sX, 0.0, X + b, ldx, sX,
+                              np));
+        const unsigned g = (unsigned)std::min<long long>((np * b * b + 255) / 256, 148LL * 32);
+        zero_blocks_kernel<<<g, 256, 0, st>>>(X + b * ldx, (long long)ldx, (long long)b, (long long)sX, (long long)np);
+        CHPL_CUDA(cudaGetLastError());
+    }
+    return CHPL_OK;
+}
+
+// X = inv(L) for X = I on entry.  n = kLeaf * 2^q: level-batched (trtri_pow2);
+// otherwise the largest such n1 < n first, X22 = inv(L22) recursively, then
+// X21 = -inv(L22) (L21 X11) as a product and a solve.
 int trtri_rec(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx)
 {
     if (n <= kLeaf) return trsm_rec(st, n, n, L, ldl, X, ldx);
-    const int64_t n1 = std::max<int64_t>(kLeaf, (n / 2) / kLeaf * kLeaf), n2 = n - n1;
-    CHPL_TRY(trtri_rec(st, n1, L, ldl, X, ldx));
+    if (leaves_pow2(n)) return trtri_pow2(st, n, L, ldl, X, ldx);
+    int64_t n1 = kLeaf;
+    while (2 * n1 < n) n1 *= 2;
+    const int64_t n2 = n - n1;
+    CHPL_TRY(trtri_pow2(st, n1, L, ldl, X, ldx));
     CHPL_TRY(trtri_rec(st, n2, L + n1 + n1 * ldl, ldl, X + n1 + n1 * ldx, ldx));
     CHPL_TRY(dgemm(st, n2, n1, n1, -1.0, L + n1, ldl, X, ldx, 0.0, X + n1, ldx));
     return trsm_rec(st, n2, n1, L + n1 + n1 * ldl, ldl, X + n1, ldx);
@@ -452,14 +524,7 @@ int dgemm(cudaStream_t st, int64_t m, int64_t n, int64_t k, double alpha, const 
         return CHPL_OK;
     }
     if (lda < std::max<int64_t>(m, 1) || ldb < std::max<int64_t>(k, 1)) { set_error("dgemm: bad leading dimension"); return CHPL_ERR_INVALID; }
-    GemmArgs a;
-    a.m = m; a.n = n; a.k = k; a.alpha = alpha; a.beta = beta;
-    a.A = A; a.lda = lda; a.B = B; a.ldb = ldb; a.C = C; a.ldc = ldc;
-    a.vecA = ((reinterpret_cast<uintptr_t>(A) & 15) == 0 && (lda & 1) == 0) ? 1 : 0;
-    a.vecB = ((reinterpret_cast<uintptr_t>(B) & 15) == 0 && (ldb & 1) == 0) ? 1 : 0;
-    if (m <= 64) return launch_gemm<64, 128, 2, 4, 2>(st, a);
-    if (n <= 32) return launch_gemm<128, 32, 4, 1, 2>(st, a);
-    return launch_gemm<128, 64, 4, 2, 2>(st, a);
+    return gemm_batched(st, m, n, k, alpha, A, lda, 0, B, ldb, 0, beta, C, ldc, 0, 1);
 }
 
 int dtrsm_llnu(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_t ldl, double* B, int64_t ldb)
@@ -491,8 +556,10 @@ int64_t dtrtri_launches(int64_t n)
 {
     if (n <= 0) return 0;
     if (n <= kLeaf) return 1;
-    const int64_t n1 = std::max<int64_t>(kLeaf, (n / 2) / kLeaf * kLeaf);
-    return dtrtri_launches(n1) + dtrtri_launches(n - n1) + 1 + trsm_count(n - n1);
+    int64_t n1 = kLeaf, levels = 0;
+    while (2 * n1 <= n) { n1 *= 2; ++levels; }   // n1 = kLeaf * 2^levels <= n
+    if (n1 == n) return 1 + 3 * levels;
+    return (1 + 3 * levels) + dtrtri_launches(n - n1) + 1 + trsm_count(n - n1);
 }
 
 int dtrsv_unn(cudaStream_t st, int64_t n, const double* U, int64_t ldu, double* x, double* work)

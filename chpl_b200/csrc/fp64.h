@@ -12,8 +12,8 @@ int dgemm(cudaStream_t st, int64_t m, int64_t n, int64_t k, double alpha, const 
           const double* B, int64_t ldb, double beta, double* C, int64_t ldc);
 // B (n x nrhs) = L^-1 B, L unit lower triangular (n x n; its upper part is not read)
 int dtrsm_llnu(cudaStream_t st, int64_t n, int64_t nrhs, const double* L, int64_t ldl, double* B, int64_t ldb);
-// X (n x n) = L^-1 for L unit lower triangular (X's upper part set to zero); one extra launch
-// (X = I) plus dtrtri_launches(n) - 1
+// X (n x n) = L^-1 for L unit lower triangular (X's upper part set to zero); it issues
+// 1 + dtrtri_launches(n) kernels (X = I first)
 int dtrtri_llnu(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx);
 int64_t dtrtri_launches(int64_t n);
 // x = U^-1 x, U upper triangular with its diagonal (n x n); work: n doubles of device scratch

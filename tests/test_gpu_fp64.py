@@ -122,11 +122,12 @@ def test_dtrsm_inverse_against_identity(cuda):
     assert np.array_equal(np.triu(Li, 1), np.zeros((n, n)))
 
 
-@pytest.mark.parametrize("n", [1, 64, 65, 200, 1024, 4096])
+@pytest.mark.parametrize("n", [1, 64, 65, 200, 1024, 2112, 3000, 4096])
 def test_dtrtri_inverse(cuda, n):
-    """inv(L) by the structured recursion: L X = I to a few ulps times n, the
-    upper part exactly zero and the diagonal exactly one (X's prior contents
-    are overwritten)."""
+    """inv(L) level by level (64 * 2^q orders: every pair of a level in one
+    batched launch) and recursively for other orders: L X = I to a few ulps
+    times n, the upper part exactly zero and the diagonal exactly one (X's
+    prior contents are overwritten)."""
     L = _unit_lower(n, np.random.default_rng(n))
     tL, pL, ldl = _buf(L)
     tX, pX, ldx = _buf(np.full((n, n), np.nan), n + 3)

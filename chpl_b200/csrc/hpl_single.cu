@@ -336,7 +336,10 @@ struct Solver {
             gemm_recs.push_back(g);
             n_launch += oz1::launches();
             const oz1::Layout y = oz1::layout((size_t)mt, (size_t)w, (size_t)k);
-            gemm_ops += 2.0 * (double)mt * (double)w * (double)y.ldk * oz1::kOz1Slices;
+            double kk = 0.0;   // K bytes the launch multiplies: diagonal d stops after (d + 1) k
+            for (int d = 0; d < oz1::kOz1Slices; ++d)
+                kk += (double)std::min<size_t>(y.ldk, round_up((size_t)(d + 1) * (size_t)k, 128));
+            gemm_ops += 2.0 * (double)mt * (double)w * kk;
             gemm_flops += 2.0 * (double)mt * (double)w * (double)k;
             ++n_emu;
             c += w;

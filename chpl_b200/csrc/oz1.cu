@@ -11,13 +11,15 @@
 //      on the tcgen05 kernel of oz2.cu (raw epilogue): A's digits are stored
 //      once per row as [A_0 | A_1 | ... | A_5] along K, and B's plane d per
 //      column as [B_d | B_(d-1) | ... | B_0 | 0 ...], so plane d of the
-//      product pairs exactly the digits whose indices add up to d;
+//      product pairs exactly the digits whose indices add up to d, and its
+//      K loop stops after the (d + 1) k non-zero bytes;
 //   4. C = alpha * 2^(ea_i + eb_j) * sum_d P_d 128^-(d+2) + beta * C, the sum
 //      taken in order d = 0, 1, ... .
 // The digits and the truncation are the reference's; the storage, the one
 // GEMM launch for all diagonals and the kernels are this library's.  It is a
-// comparison engine (slower than Ozaki-II, as in the reference: every
-// diagonal's product runs over the full 6k of K, half of it against zeros).
+// comparison engine (slower than Ozaki-II, as in the reference): the launch
+// runs 21 digit products' worth of K blocks (1 + 2 + ... + 6 of k each), the
+// method's own count, against 11 modulus products of Ozaki-II.
 #include <algorithm>
 
 #include "common.cuh"
@@ -190,9 +192,10 @@ int gemm(cudaStream_t st, size_t m, size_t n, size_t k, double alpha, const doub
     zero_tail_kernel<<<(unsigned)(kOz1Slices * y.nPad), 128, 0, st>>>(rb, (int)(kOz1Slices * y.nPad), (int)y.ldk,
                                                                       kOz1Slices * ki);
     CHPL_CUDA(cudaGetLastError());
-    // one raw launch: plane d = diagonal d; A's plane stride 0 (every plane reads the same digit rows)
+    // one raw launch: plane d = diagonal d; A's plane stride 0 (every plane reads the same digit
+    // rows), and plane d stops after its (d + 1) k non-zero bytes of K
     CHPL_TRY(oz2::gemm_launch(st, 1, m, n, y.ldk, (unsigned)kOz1Slices, ra, y.mPad, rb, y.nPad, nullptr, nullptr, 0.0,
-                              0.0, nullptr, 0, P, m, nullptr, oz2::num_sms(), 0));
+                              0.0, nullptr, 0, P, m, nullptr, oz2::num_sms(), 0, (long long)k));
     const long long tot = (long long)m * n;
     const unsigned g = (unsigned)std::min<long long>((tot + 255) / 256, 148LL * 32);
     recon_kernel<<<g, 256, 0, st>>>(C, (long long)ldc, mi, ni, P, (long long)m, ea, eb, alpha, beta);

@@ -295,6 +295,7 @@ struct Form {
 struct GemmParams {
     int m, n;
     int mtiles, ntiles, kblocks;
+    int kstep;          // > 0: plane l stops after (l + 1) * kstep bytes of K (the rest of its B rows is zero)
     int rowsA, rowsB;   // padded rows per modulus plane in the residue buffers
     int planeA;         // row offset between A's planes: rowsA, or 0 when every plane reads the same rows
     int mode;           // 0: CRT into C; 1: raw int32 products into P
@@ -335,6 +336,13 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, uin
 {
     int never = 0;
     return mbar_wait(bar, parity, &never, limit_ns);
+}
+
+// K blocks of plane l: all of them, or with p.kstep > 0 the ones that hold the
+// plane's non-zero (l + 1) * kstep bytes (producer and MMA issuer agree on it)
+__device__ __forceinline__ int plane_kblocks(const GemmParams& p, int l)
+{
+    return p.kstep > 0 ? min(p.kblocks, ((l + 1) * p.kstep + BK - 1) / BK) : p.kblocks;
 }
 
 __device__ __forceinline__ void spin_ns(uint64_t ns)
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int rowA = mt * F::TBM + (int)rank * BM;
                 const int rowB = nt * BN + (int)rank * F::B_ROWS;
                 for (int l = 0; l < L && ok; ++l)
-                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                    for (int kb = 0; kb < plane_kblocks(p, l); ++kb) {
                         if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag)) { ok = false; break; }
                         uint8_t* sa = smem + stage * STAGE_BYTES;
                         if (PAIR) {
@@ -450,7 +458,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!mbar_wait(&acc_empty[buf], aph ^ 1u, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d = tmem_base + buf * BN;
-                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                    for (int kb = 0; kb < plane_kblocks(p, l); ++kb) {
                         if (!mbar_wait(&full[stage], ph, abort_flag)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t a0 = smem_u32(smem + stage * STAGE_BYTES), b0 = a0 + A_BYTES;
@@ -784,7 +792,7 @@ static int max_pair_clusters()
 int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsigned L, const int8_t* ra, size_t rowsA,
                 const int8_t* rb, size_t rowsB, const int32_t* shiftA, const int32_t* shiftB, double alpha,
                 double beta, double* C, size_t ldc, int32_t* P, size_t ldp, int8_t* scratch, int grid_max,
-                long long planeA)
+                long long planeA, long long kstep)
 {
     const Moduli* M = moduli((int)L);
     if (!M) { set_error("bad num_moduli"); return CHPL_ERR_INVALID; }
@@ -807,6 +815,8 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     p.mtiles = (int)((m + tbm - 1) / tbm);
     p.ntiles = (int)((n + BN - 1) / BN);
     p.kblocks = (int)(kPad / BK);
+    if (kstep < 0 || kstep > (long long)kPad) { set_error("gemm_launch: bad plane K step"); return CHPL_ERR_INVALID; }
+    p.kstep = (int)kstep;
     p.rowsA = (int)rowsA;
     p.planeA = (int)planeA;
     p.rowsB = (int)rowsB;

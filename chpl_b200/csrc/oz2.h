@@ -44,7 +44,8 @@ int split(cudaStream_t st, bool contiguous, const double* x, size_t ld, size_t n
 int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsigned L, const int8_t* ra, size_t rowsA,
                 const int8_t* rb, size_t rowsB, const int32_t* shiftA, const int32_t* shiftB, double alpha,
                 double beta, double* C, size_t ldc, int32_t* P, size_t ldp, int8_t* scratch, int grid_max,
-                long long planeA = -1);   // A's plane stride in rows: -1 = rowsA; 0 = every plane reads the same rows
+                long long planeA = -1,    // A's plane stride in rows: -1 = rowsA; 0 = every plane reads the same rows
+                long long kstep = 0);     // > 0: plane l multiplies only its first (l + 1) * kstep bytes of K
 int scale(cudaStream_t st, double* C, size_t ldc, size_t m, size_t n, double beta);
 int read_clear_status(int* st);
 

@@ -55,6 +55,13 @@ def test_host_only_entry_points():
     assert L.chpl_oz2_shift_bits(11, 4096, ctypes.byref(a), ctypes.byref(b)) == 0
     assert (a.value, b.value) == (43, 43)
     assert L.chpl_laswp_work_bytes(1000, 1024) >= 2 * 1024 * 8
+    # Ozaki-I: digits of A (1024 x 6k) and B (6 planes of 512 x 6k), six int32 products of m x n
+    w = ctypes.c_size_t()
+    assert L.chpl_oz1_worksize(1000, 300, 4096, ctypes.byref(w)) == 0
+    assert w.value >= 1024 * 6 * 4096 + 6 * 512 * 6 * 4096 + 6 * 1000 * 300 * 4
+    assert L.chpl_oz1_worksize(64, 64, 21845, ctypes.byref(w)) == 0
+    assert L.chpl_oz1_worksize(64, 64, 21846, ctypes.byref(w)) == _lib.CHPL_ERR_UNSUPPORTED
+    assert L.chpl_oz1_worksize(64, 64, 64, None) == _lib.CHPL_ERR_INVALID
 
 
 def test_shift_bits_agree_with_oracle():
@@ -81,6 +88,9 @@ def test_gemm_entry_points_validate_before_early_return():
     rc = L.chpl_oz2_gemm(None, 0, 0, 4, 4, 131072, ctypes.byref(a), None, 4, None, 131072, ctypes.byref(b), None, 4, 11,
                          1, None, None, None, 0, 0, 0, 0, None)
     assert rc == _lib.CHPL_ERR_UNSUPPORTED
+    # Ozaki-I: leading dimensions and NULL matrices are checked before any CUDA call
+    assert L.chpl_oz1_gemm(None, 8, 8, 8, -1.0, None, 4, None, 8, 1.0, None, 8, None) == _lib.CHPL_ERR_INVALID
+    assert L.chpl_oz1_gemm(None, 8, 8, 8, -1.0, None, 8, None, 8, 1.0, None, 8, None) == _lib.CHPL_ERR_INVALID
 
 
 def test_default_config():

@@ -107,6 +107,15 @@ struct Solver {
     double* Linv[2] = {nullptr, nullptr};  // inv(L) of a super-block's unit lower triangle (K x K), by parity
     void* wLinv[2] = {nullptr, nullptr};   // residues of inv(L) (A part, k = K), by parity
     bool emu_trsm = false;                 // U12 = inv(L) * A12 through the emulated GEMM
+    // host ingest (a system in host memory, serial schedule): [A | b] arrives on its own copy
+    // stream in column chunks while the factorization runs on the chunks already present
+    bool ingest = false;
+    cudaStream_t sC = nullptr;
+    std::vector<int64_t> in_bound;         // chunk c = columns [in_bound[c], in_bound[c + 1])
+    std::vector<cudaEvent_t> in_ev;        // chunk c has landed
+    std::vector<void*> lw_old;             // laswp plans of an earlier super-block, rebuilt for a late chunk
+    double* Linv_old = nullptr;            // inv(L) of an earlier super-block and its residues, the same
+    void* wLinv_old = nullptr;
     void* w0 = nullptr;                    // oz2 B part + scratch for s0
     void* wP = nullptr;                    // oz2 B part + scratch for sP
     int64_t chunk = 0;
@@ -178,8 +187,12 @@ struct Solver {
         const int npl = (int)((K + NB - 1) / NB);
         const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0) + oz1b * (cfg.lookahead ? 2 : 1);
         const size_t pbytes = panel_work_bytes(N, NB);
-        const size_t need = bytesA + ozbytes + pbytes + 2 * npl * laswp_work_bytes(NB) + (size_t)(3 * N + 64) * 8 +
-                            ((size_t)768 << 20);
+        size_t linv_res = 0;   // residues of one inv(L) (A part, k = K)
+        if (emu_trsm)
+            CHPL_TRY(chpl_oz2_worksize((size_t)K, 256, (size_t)K, (unsigned)cfg.moduli, 1, 0, &tot, &linv_res, nullptr));
+        const size_t linv_bytes = emu_trsm ? (size_t)K * K * sizeof(double) + linv_res : 0;
+        const size_t need = bytesA + ozbytes + pbytes + (ingest ? 3 : 2) * (npl * laswp_work_bytes(NB) + linv_bytes) +
+                            (size_t)(3 * N + 64) * 8 + ((size_t)768 << 20);
         if (cfg.verbose)
             std::printf("MEM PLAN: matrix %.2f GiB | oz2 work %.2f GiB | getrf %.3f GiB | total %.2f GiB vs free %.2f GiB"
                         " | K=%" PRId64 " (agg %d) reserve %d SMs\n",
@@ -200,15 +213,21 @@ struct Solver {
             lw[b].assign(npl, nullptr);
             for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw[b][p], laswp_work_bytes(NB)));
         }
+        if (ingest) {
+            lw_old.assign(npl, nullptr);
+            for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw_old[p], laswp_work_bytes(NB)));
+        }
         if (a_big) {
             for (int b = 0; b < 2; ++b) CHPL_CUDA(cudaMalloc(&wA[b], a_big));
             CHPL_CUDA(cudaMalloc(&wAin, a_in));
             if (emu_trsm) {
-                size_t tl = 0, al = 0;
-                CHPL_TRY(chpl_oz2_worksize((size_t)K, 256, (size_t)K, (unsigned)cfg.moduli, 1, 0, &tl, &al, nullptr));
                 for (int b = 0; b < 2; ++b) {
                     CHPL_CUDA(cudaMalloc((void**)&Linv[b], (size_t)K * K * sizeof(double)));
-                    CHPL_CUDA(cudaMalloc(&wLinv[b], al));
+                    CHPL_CUDA(cudaMalloc(&wLinv[b], linv_res));
+                }
+                if (ingest) {
+                    CHPL_CUDA(cudaMalloc((void**)&Linv_old, (size_t)K * K * sizeof(double)));
+                    CHPL_CUDA(cudaMalloc(&wLinv_old, linv_res));
                 }
             }
             CHPL_CUDA(cudaMalloc(&w0, cfg.lookahead ? rest0 : std::max(rest0, restP)));
@@ -225,6 +244,12 @@ struct Solver {
 
     void destroy()
     {
+        if (sC) cudaStreamSynchronize(sC);
+        for (auto e : in_ev) cudaEventDestroy(e);
+        if (sC) cudaStreamDestroy(sC);
+        for (void* p : lw_old) if (p) cudaFree(p);
+        if (Linv_old) cudaFree(Linv_old);
+        if (wLinv_old) cudaFree(wLinv_old);
         for (auto e : ev_pool) cudaEventDestroy(e);
         if (wP && wP != w0) cudaFree(wP);
         if (w0) cudaFree(w0);
@@ -415,22 +440,27 @@ struct Solver {
     int invert_l(int64_t s)
     {
         if (!emu_trsm) return CHPL_OK;
+        return invert_l_into(sP, s, Linv[s & 1], wLinv[s & 1]);
+    }
+
+    // Li = inv(L11) of super-block s (unit lower), then its residues (A part, k = K) into wli
+    int invert_l_into(cudaStream_t st, int64_t s, double* Li, void* wli)
+    {
         const int64_t J = sb_start(s), KJ = sb_width(s);
-        double* Li = Linv[s & 1];
         PhaseTimer::Rec r;
-        CHPL_TRY(clk.begin(sP, PH_TRSM, r));
-        CHPL_TRY(dtrtri_llnu(sP, KJ, at(J, J), ld, Li, KJ));
+        CHPL_TRY(clk.begin(st, PH_TRSM, r));
+        CHPL_TRY(dtrtri_llnu(st, KJ, at(J, J), ld, Li, KJ));
         n_launch += 1 + dtrtri_launches(KJ);
-        CHPL_TRY(clk.end(sP, r));
+        CHPL_TRY(clk.end(st, r));
         const oz2::Moduli* M = oz2::moduli(cfg.moduli);
         const oz2::Layout y = oz2::layout((size_t)KJ, 256, (size_t)KJ, cfg.moduli, true, false);
-        uint8_t* pa = static_cast<uint8_t*>(wLinv[s & 1]);
-        CHPL_TRY(clk.begin(sP, PH_SPLIT, r));
-        CHPL_TRY(oz2::split(sP, false, Li, (size_t)KJ, (size_t)KJ, (size_t)KJ, cfg.moduli, M->alpha,
+        uint8_t* pa = static_cast<uint8_t*>(wli);
+        CHPL_TRY(clk.begin(st, PH_SPLIT, r));
+        CHPL_TRY(oz2::split(st, false, Li, (size_t)KJ, (size_t)KJ, (size_t)KJ, cfg.moduli, M->alpha,
                             reinterpret_cast<int8_t*>(pa + y.a_res), y.mPad, y.kPad, reinterpret_cast<int32_t*>(pa + y.a_shift),
-                            static_cast<uint8_t*>(wP) + y.tmp_off));
+                            static_cast<uint8_t*>(st == s0 ? w0 : wP) + y.tmp_off));
         n_launch += 5;
-        CHPL_TRY(clk.end(sP, r));
+        CHPL_TRY(clk.end(st, r));
         return CHPL_OK;
     }
     int cap_bulk_cur = 0, cap_chain_cur = 0;
@@ -446,6 +476,87 @@ struct Solver {
     {
         const int64_t c2 = std::min(N, sb_start(s) + sb_width(s) + sb_width(s + 1));
         return cfg.lookahead && reserve > 0 && (N - c2) >= 8 * K;
+    }
+
+    // Enqueue [A | b] from host memory (leading dimension ldab) on the copy stream in column
+    // chunks of 2K, 4K, 8K, ... columns (multiples of the super-block width K, the last one
+    // ending at column N), each followed by its event.  The copies start once `start` has
+    // been reached on s0.
+    int ingest_enqueue(const double* Ab, size_t ldab, cudaEvent_t start)
+    {
+        CHPL_CUDA(cudaStreamCreateWithFlags(&sC, cudaStreamNonBlocking));
+        CHPL_CUDA(cudaStreamWaitEvent(sC, start, 0));
+        in_bound.assign(1, 0);
+        for (int64_t w = 2 * K; in_bound.back() < ncols; w *= 2)
+            in_bound.push_back(std::min<int64_t>(ncols, in_bound.back() + w));
+        for (size_t c = 0; c + 1 < in_bound.size(); ++c) {
+            const int64_t a = in_bound[c], b = in_bound[c + 1];
+            CHPL_CUDA(cudaMemcpy2DAsync(at(0, a), (size_t)ld * sizeof(double), Ab + (size_t)a * ldab,
+                                        ldab * sizeof(double), (size_t)N * sizeof(double), (size_t)(b - a),
+                                        cudaMemcpyHostToDevice, sC));
+            cudaEvent_t e;
+            CHPL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            in_ev.push_back(e);
+            CHPL_CUDA(cudaEventRecord(e, sC));
+        }
+        return CHPL_OK;
+    }
+
+    // Super-block t's interchanges, U12 and trailing update on the columns [c0, c0 + nc), on s0.
+    // live: t is the super-block factored last (its plans and inv(L) residues are current);
+    // otherwise they are rebuilt from ipiv and L11(t), which the matrix still holds, and give
+    // the same values.
+    int apply_step(int64_t t, bool live, int64_t c0, int64_t nc)
+    {
+        if (nc <= 0) return CHPL_OK;
+        const int64_t J = sb_start(t), KJ = sb_width(t);
+        std::vector<void*>& plans = live ? lw[t & 1] : lw_old;
+        for (int64_t p = 0; J + p * NB < J + KJ; ++p) {
+            const int64_t jp = J + p * NB, nb = std::min(NB, J + KJ - jp);
+            if (!live) {
+                CHPL_TRY(laswp_plan(s0, ipiv, jp, jp + nb, plans[p]));
+                n_launch += 2;
+            }
+            CHPL_TRY(laswp_cols(s0, plans[p], nb, c0, nc));
+        }
+        if (!emu_trsm) CHPL_TRY(trsm(s0, J, KJ, c0, nc));
+        else {
+            double* Li = live ? Linv[t & 1] : Linv_old;
+            void* wli = live ? wLinv[t & 1] : wLinv_old;
+            if (!live) CHPL_TRY(invert_l_into(s0, t, Li, wli));
+            CHPL_TRY(emu(s0, w0, wli, false, KJ, KJ, Li, KJ, J, c0, nc, at(J, c0), 1.0, 0.0, 0));
+        }
+        return update(s0, w0, wA[0], true, J + KJ, J, KJ, c0, nc, 0);
+    }
+
+    // The serial factorization over a matrix still arriving (ingest_enqueue): before super-block
+    // s is factored, every chunk up to its last column is taken in, each catching up on the
+    // steps 0..s-1 the columns already present have received; then step s runs on all columns
+    // present.  Every column gets the same operations in the same order as in
+    // factor_and_solve's serial schedule, so the results are bit-identical to it.
+    int factor_and_solve_ingest()
+    {
+        const int64_t nsb = (N + K - 1) / K;
+        int64_t ready = 0;   // columns [0, ready) are present and up to date with the steps issued
+        size_t c = 0;
+        for (int64_t s = 0; s < nsb; ++s) {
+            const int64_t J = sb_start(s), KJ = sb_width(s), c1 = J + KJ;
+            while (c < in_ev.size() && (ready < c1 || s == nsb - 1)) {
+                CHPL_CUDA(cudaStreamWaitEvent(s0, in_ev[c], 0));
+                const int64_t a = in_bound[c], b = in_bound[c + 1];
+                for (int64_t t = 0; t < s; ++t) CHPL_TRY(apply_step(t, false, a, b - a));
+                ready = b;
+                ++c;
+            }
+            CHPL_TRY(factor_superblock(s, 0));
+            CHPL_TRY(apply_step(s, true, c1, ready - c1));
+        }
+        PhaseTimer::Rec r;
+        CHPL_TRY(clk.begin(s0, PH_SOLVE, r));
+        CHPL_TRY(dtrsv_unn(s0, N, A, ld, at(0, N), xwork));
+        n_launch += dtrsv_launches(N);
+        CHPL_TRY(clk.end(s0, r));
+        return CHPL_OK;
     }
 
     int factor_and_solve()
@@ -538,6 +649,8 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
         return CHPL_ERR_INVALID;
     }
     Solver s;
+    // a system in host memory streams in while the serial schedule factors what has arrived
+    s.ingest = Ab != nullptr && !cfg->lookahead;
     int rc = s.init(*cfg);
     if (rc != CHPL_OK) { s.destroy(); return rc; }
     double* xs = nullptr;   // x kept aside while [A | b] is copied in again for the residual
@@ -552,18 +665,23 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     cudaEvent_t g0 = ev.e[0], g1 = ev.e[1], t0 = ev.e[2], t1 = ev.e[3];
     const size_t row_bytes = (size_t)s.N * sizeof(double);
     cudaEventRecord(g0, s.s0);
-    if (Ab) {
+    if (Ab && !s.ingest) {
         cudaError_t e = cudaMemcpy2DAsync(s.A, (size_t)s.ld * sizeof(double), Ab, ldab * sizeof(double), row_bytes,
                                           (size_t)s.ncols, cudaMemcpyHostToDevice, s.s0);
         if (e != cudaSuccess) return finish(cuda_fail(e, "[A|b] host to device", __FILE__, __LINE__));
-    } else {
+    } else if (!Ab) {
         rc = matgen(s.s0, s.A, (size_t)s.ld, (size_t)s.N, (size_t)s.ncols, 0, 0, s.ncols, cfg->seed, cfg->generator);
         if (rc != CHPL_OK) return finish(rc);
     }
     cudaEventRecord(g1, s.s0);
     cudaEventRecord(t0, s.s0);
     cudaStreamWaitEvent(s.sP, t0, 0);
-    rc = s.factor_and_solve();
+    if (s.ingest) {   // the timed region then covers the host-to-device copy as well
+        rc = s.ingest_enqueue(Ab, ldab, t0);
+        if (rc == CHPL_OK) rc = s.factor_and_solve_ingest();
+    } else {
+        rc = s.factor_and_solve();
+    }
     if (rc != CHPL_OK) { cudaDeviceSynchronize(); return finish(rc); }
     cudaEventRecord(t1, s.s0);
     cudaError_t e = cudaEventSynchronize(t1);

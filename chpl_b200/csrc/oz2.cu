@@ -296,6 +296,8 @@ struct GemmParams {
     int m, n;
     int mtiles, ntiles, kblocks;
     int kstep;          // > 0: plane l stops after (l + 1) * kstep bytes of K (the rest of its B rows is zero)
+    int magic[kMaxModuli];            // ceil(2^32 / m_l): the epilogue's residue estimate
+    unsigned long long crt_bias;      // -128 * sum_l v_l mod 2^64: removes the residues' +128 bias
     int rowsA, rowsB;   // padded rows per modulus plane in the residue buffers
     int planeA;         // row offset between A's planes: rowsA, or 0 when every plane reads the same rows
     int mode;           // 0: CRT into C; 1: raw int32 products into P
@@ -322,14 +324,18 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& 
     nt = local / gsz;
 }
 
-__device__ __forceinline__ int residue_i32(int x, int mod, int hi, float inv)
+// Symmetric residue of an int32 accumulator modulo m (129 <= m <= 256): q =
+// floor(x * magic / 2^32) with magic = ceil(2^32 / m) is floor(x / m) to within
+// one either way (|x| < 2^31 keeps the estimate's error below 1/2), so x - q m
+// lies in [-m, 2m) and three conditional steps give [hi - m + 1, hi].  Integer
+// multiply-adds only: no int <-> float conversions.
+__device__ __forceinline__ int residue_i32(int x, int mod, int hi, int magic)
 {
     if (mod == 256) return (int)(int8_t)(x & 0xff);
-    const int q = __float2int_rn(__int2float_rn(x) * inv);
-    int r = x - q * mod;
-    r = (r > hi) ? r - mod : r;
-    r = (r < hi - mod + 1) ? r + mod : r;
-    return r;
+    int r = x - __mulhi(x, magic) * mod;
+    r += (r < 0) ? mod : 0;
+    r -= (r >= mod) ? mod : 0;
+    return (r > hi) ? r - mod : r;
 }
 
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns)
@@ -527,7 +533,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         asm volatile("prefetch.global.L2 [%0];" ::"l"(cp + (size_t)j * p.ldc));
                 }
                 const int mod = p.M.mod[l], hi = p.M.hi[l];
-                const float inv = p.M.inv_f[l];
+                const int magic = p.magic[l];
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     uint32_t v[32];
@@ -550,13 +556,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 if (gj0 + j < p.n) dst[(size_t)(gj0 + j) * p.ldp] = (int32_t)v[j];
                         }
                     } else {
+                        // residues biased by +128 into bytes 0..255 (the CRT removes the bias)
                         uint32_t w[8];
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
                             uint32_t x = 0;
 #pragma unroll
                             for (int t = 0; t < 4; ++t)
-                                x |= ((uint32_t)residue_i32((int)v[4 * q + t], mod, hi, inv) & 0xffu) << (8 * t);
+                                x |= (uint32_t)(residue_i32((int)v[4 * q + t], mod, hi, magic) + 128) << (8 * t);
                             w[q] = x;
                         }
                         uint4* dst = reinterpret_cast<uint4*>(scr + (((size_t)l * 8 + half * 4 + c) * BM + row) * 32);
@@ -589,9 +596,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int l = 0; l < kMaxModuli; ++l)
                         if (l < L) w[l] = __ldcg(reinterpret_cast<const uint4*>(sp + (size_t)l * 8 * BM * 32));
+                    // S = sum_l r_l v_l mod 2^64 = sum_l (r_l + 128) v_l - 128 sum_l v_l: the
+                    // biased bytes multiply unsigned (one wide multiply-add per term)
                     unsigned long long S[16];
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) S[t] = 0ull;
+                    for (int t = 0; t < 16; ++t) S[t] = p.crt_bias;
 #pragma unroll
                     for (int l = 0; l < kMaxModuli; ++l) {
                         if (l < L) {
@@ -599,8 +608,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const uint32_t ws[4] = {w[l].x, w[l].y, w[l].z, w[l].w};
 #pragma unroll
                             for (int t = 0; t < 16; ++t) {
-                                const int r = (int)(int8_t)((ws[t >> 2] >> (8 * (t & 3))) & 0xffu);
-                                S[t] += (unsigned long long)(long long)r * vl;
+                                const uint32_t u = (ws[t >> 2] >> (8 * (t & 3))) & 0xffu;
+                                S[t] += (unsigned long long)u * vl;
                             }
                         }
                     }
@@ -608,7 +617,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int t = 0; t < 16; ++t) {
                         const int gj = gj0 + t;
                         if (gj < p.n) {
-                            const double prod = scalbn((double)(long long)S[t] * p.M.Mf, -(sa + __ldg(&p.shiftB[gj])));
+                            // prod * 2^-e: one exact power-of-two multiply (rounded once, as
+                            // scalbn) while 2^-e is a normal double
+                            const int e = sa + __ldg(&p.shiftB[gj]);
+                            double prod = (double)(long long)S[t] * p.M.Mf;
+                            prod = (e >= -1022 && e <= 1022) ? prod * __longlong_as_double((long long)(1023 - e) << 52)
+                                                             : scalbn(prod, -e);
                             __stcs(cbase + (size_t)t * p.ldc, readc ? fma(p.alpha, prod, p.beta * cv[t]) : p.alpha * prod);
                         }
                     }
@@ -833,6 +847,11 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     p.beta = beta;
     p.scratch = scratch;
     p.M = *M;
+    p.crt_bias = 0;
+    for (unsigned l = 0; l < L; ++l) {
+        p.magic[l] = (int)((0x100000000ull + (unsigned long long)M->mod[l] - 1) / (unsigned long long)M->mod[l]);
+        p.crt_bias -= 128ull * M->v[l];
+    }
     const int tiles = p.mtiles * p.ntiles;
     if (!pair) {
         const int grid = std::min(tiles, grid_max);

@@ -329,12 +329,17 @@ int chpl_hpl_run(const chpl_hpl_config *cfg, chpl_hpl_result *res, double *x_out
  * device (P = Q = 1): [A | b] (N x (N+1), column-major, ldab >= N, b = column
  * N) is copied to the device (page-locked memory from chpl_host_alloc copies
  * at full bandwidth; pageable memory works, slower), factored and solved with
- * the same kernels and schedule as chpl_hpl_run (cfg->seed is unused), and x
- * is written to x_out (host, N doubles; may be NULL).  verify = 1 copies
- * [A | b] in again after the solve and computes the HPL scaled residual
- * against it (res->resid, res->passed); verify = 0 leaves res->resid NaN and
- * res->passed 0.  res->time_s is factor + solve (device time), res->matgen_s
- * the host-to-device copy of [A | b].  The host-buffer form of run_case
+ * the same kernels as chpl_hpl_run (cfg->seed is unused), and x is written to
+ * x_out (host, N doubles; may be NULL).  With the serial schedule
+ * (cfg->lookahead = 0) the copy runs in column chunks on its own stream while
+ * the factorization works on the columns already present (a late chunk first
+ * catches up on the steps the others have received); x is bit-identical to
+ * chpl_hpl_run's on the same system, and res->time_s covers copy + factor +
+ * solve (device time, res->matgen_s = 0).  With the lookahead the system is
+ * copied first (res->matgen_s) and res->time_s is factor + solve.  verify = 1
+ * copies [A | b] in again after the solve and computes the HPL scaled
+ * residual against it (res->resid, res->passed); verify = 0 leaves
+ * res->resid NaN and res->passed 0.  The host-buffer form of run_case
  * (src/chpl_single.cu:733-840), whose input the reference always generates
  * on the device (src/chpl_single.cu:750).
  */

@@ -15,7 +15,9 @@ from __future__ import annotations
 
 import argparse
 import json
+import time
 
+import numpy as np
 import torch
 
 from . import hpl, oz2
@@ -125,6 +127,23 @@ def panel_case(m: int, n: int, reps: int) -> dict:
     return {"case": "panel", "m": m, "n": n, "ms": best * 1e3, "fp64_tflops": fl / best / 1e12, "info": int(info.item())}
 
 
+def ingest_case(N: int, NB: int, L: int) -> dict:
+    """The same system solved from device-generated input and from pinned host
+    memory (the copy streamed in by column chunks): device times, phases and the
+    chunk timeline (printed by the library with verbose = 1)."""
+    cfg = hpl.Config(N=N, NB=NB, moduli=L)
+    a = hpl.run(cfg, want_x=True)
+    with hpl.HostSystem(N) as S:
+        S.generate(cfg.seed)
+        vcfg = hpl.Config(N=N, NB=NB, moduli=L, verbose=True)
+        t0 = time.perf_counter()
+        b = hpl.run_host(vcfg, S, verify=False)
+        wall = time.perf_counter() - t0
+    return {"case": "ingest", "N": N, "NB": NB, "moduli": L, "resident_s": a.time_s, "host_s": b.time_s,
+            "host_wall_s": wall, "x_equal": bool(np.array_equal(a.x, b.x)),
+            "phases_resident": a.phases, "phases_host": b.phases}
+
+
 def laswp_case(rows: int, cols: int, swaps: int, reps: int) -> dict:
     """Interchanges of `swaps` partial-pivoting rows (ipiv[i] uniform in [i, rows))
     on a rows x cols column-major matrix: plan + apply, as the solver's
@@ -215,6 +234,10 @@ def main() -> None:
         f.add_argument("--n", type=int, default=8192)
         f.add_argument("--k", type=int, default=8192)
         f.add_argument("--reps", type=int, default=5)
+    ig = sub.add_parser("ingest", help="host-buffer solve (streamed copy) beside the device-generated one")
+    ig.add_argument("--N", type=int, default=139264)
+    ig.add_argument("--NB", type=int, default=1024)
+    ig.add_argument("--moduli", type=int, default=11)
     pn = sub.add_parser("panel")
     pn.add_argument("--m", type=int, default=65536)
     pn.add_argument("--n", type=int, default=1024)
@@ -253,6 +276,8 @@ def main() -> None:
         print(json.dumps(fp64_case(a.what, a.m, a.n, a.k, a.reps)), flush=True)
     elif a.what == "panel":
         print(json.dumps(panel_case(a.m, a.n, a.reps)), flush=True)
+    elif a.what == "ingest":
+        print(json.dumps(ingest_case(a.N, a.NB, a.moduli)), flush=True)
     elif a.what == "laswp":
         print(json.dumps(laswp_case(a.rows, a.cols, a.swaps, a.reps)), flush=True)
     else:

@@ -113,6 +113,8 @@ struct Solver {
     cudaStream_t sC = nullptr;
     std::vector<int64_t> in_bound;         // chunk c = columns [in_bound[c], in_bound[c + 1])
     std::vector<cudaEvent_t> in_ev;        // chunk c has landed
+    std::vector<cudaEvent_t> in_take;      // s0 reached chunk c's wait (verbose runs: timed events)
+    std::vector<int64_t> in_step;          // the step chunk c was taken in at
     std::vector<void*> lw_old;             // laswp plans of an earlier super-block, rebuilt for a late chunk
     double* Linv_old = nullptr;            // inv(L) of an earlier super-block and its residues, the same
     void* wLinv_old = nullptr;
@@ -246,6 +248,7 @@ struct Solver {
     {
         if (sC) cudaStreamSynchronize(sC);
         for (auto e : in_ev) cudaEventDestroy(e);
+        for (auto e : in_take) cudaEventDestroy(e);
         if (sC) cudaStreamDestroy(sC);
         for (void* p : lw_old) if (p) cudaFree(p);
         if (Linv_old) cudaFree(Linv_old);
@@ -495,7 +498,7 @@ struct Solver {
                                         ldab * sizeof(double), (size_t)N * sizeof(double), (size_t)(b - a),
                                         cudaMemcpyHostToDevice, sC));
             cudaEvent_t e;
-            CHPL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            CHPL_CUDA(cudaEventCreateWithFlags(&e, cfg.verbose ? cudaEventDefault : cudaEventDisableTiming));
             in_ev.push_back(e);
             CHPL_CUDA(cudaEventRecord(e, sC));
         }
@@ -542,6 +545,13 @@ struct Solver {
         for (int64_t s = 0; s < nsb; ++s) {
             const int64_t J = sb_start(s), KJ = sb_width(s), c1 = J + KJ;
             while (c < in_ev.size() && (ready < c1 || s == nsb - 1)) {
+                if (cfg.verbose) {
+                    cudaEvent_t e;
+                    CHPL_CUDA(cudaEventCreate(&e));
+                    CHPL_CUDA(cudaEventRecord(e, s0));
+                    in_take.push_back(e);
+                    in_step.push_back(s);
+                }
                 CHPL_CUDA(cudaStreamWaitEvent(s0, in_ev[c], 0));
                 const int64_t a = in_bound[c], b = in_bound[c + 1];
                 for (int64_t t = 0; t < s; ++t) CHPL_TRY(apply_step(t, false, a, b - a));
@@ -689,6 +699,17 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     float ms_gen = 0.f, ms = 0.f;
     cudaEventElapsedTime(&ms_gen, g0, g1);
     cudaEventElapsedTime(&ms, t0, t1);
+    if (s.ingest && cfg->verbose) {   // when each chunk landed and when the factorization reached it
+        for (size_t c = 0; c < s.in_take.size() && c < s.in_ev.size(); ++c) {
+            float landed = 0.f, reached = 0.f;
+            cudaEventElapsedTime(&landed, t0, s.in_ev[c]);
+            cudaEventElapsedTime(&reached, t0, s.in_take[c]);
+            std::printf("INGEST: chunk %zu columns [%" PRId64 ", %" PRId64 ") landed %.1f ms, reached at step %" PRId64
+                        " %.1f ms\n",
+                        c, s.in_bound[c], s.in_bound[c + 1], landed, s.in_step[c], reached);
+        }
+        std::fflush(stdout);
+    }
     int hinfo = 0;
     cudaMemcpy(&hinfo, s.info + 1, sizeof(int), cudaMemcpyDeviceToHost);
     int perr = 0;

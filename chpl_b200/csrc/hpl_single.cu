@@ -113,8 +113,9 @@ struct Solver {
     cudaStream_t sC = nullptr;
     std::vector<int64_t> in_bound;         // chunk c = columns [in_bound[c], in_bound[c + 1])
     std::vector<cudaEvent_t> in_ev;        // chunk c has landed
-    std::vector<cudaEvent_t> in_take;      // s0 reached chunk c's wait (verbose runs: timed events)
-    std::vector<int64_t> in_step;          // the step chunk c was taken in at
+    std::vector<cudaEvent_t> in_take;      // s0 reached an intake's waits (verbose runs: timed events)
+    std::vector<int64_t> in_step;          // its step
+    std::vector<size_t> in_first, in_last; // its chunks
     std::vector<void*> lw_old;             // laswp plans of an earlier super-block, rebuilt for a late chunk
     double* Linv_old = nullptr;            // inv(L) of an earlier super-block and its residues, the same
     void* wLinv_old = nullptr;
@@ -482,16 +483,14 @@ struct Solver {
     }
 
     // Enqueue [A | b] from host memory (leading dimension ldab) on the copy stream in column
-    // chunks of 2K, 4K, 8K, ... columns (multiples of the super-block width K, the last one
-    // ending at column N), each followed by its event.  The copies start once `start` has
-    // been reached on s0.
+    // chunks of 2K columns (two super-blocks; the last chunk ends at column N), each followed
+    // by its event.  The copies start once `start` has been reached on s0.
     int ingest_enqueue(const double* Ab, size_t ldab, cudaEvent_t start)
     {
         CHPL_CUDA(cudaStreamCreateWithFlags(&sC, cudaStreamNonBlocking));
         CHPL_CUDA(cudaStreamWaitEvent(sC, start, 0));
         in_bound.assign(1, 0);
-        for (int64_t w = 2 * K; in_bound.back() < ncols; w *= 2)
-            in_bound.push_back(std::min<int64_t>(ncols, in_bound.back() + w));
+        while (in_bound.back() < ncols) in_bound.push_back(std::min<int64_t>(ncols, in_bound.back() + 2 * K));
         for (size_t c = 0; c + 1 < in_bound.size(); ++c) {
             const int64_t a = in_bound[c], b = in_bound[c + 1];
             CHPL_CUDA(cudaMemcpy2DAsync(at(0, a), (size_t)ld * sizeof(double), Ab + (size_t)a * ldab,
@@ -532,31 +531,38 @@ struct Solver {
         return update(s0, w0, wA[0], true, J + KJ, J, KJ, c0, nc, 0);
     }
 
-    // The serial factorization over a matrix still arriving (ingest_enqueue): before super-block
-    // s is factored, every chunk up to its last column is taken in, each catching up on the
-    // steps 0..s-1 the columns already present have received; then step s runs on all columns
-    // present.  Every column gets the same operations in the same order as in
-    // factor_and_solve's serial schedule, so the results are bit-identical to it.
+    // The serial factorization over a matrix still arriving (ingest_enqueue).  Before
+    // super-block s is factored, the chunks holding its columns are taken in, together with
+    // every later chunk whose copy has already completed when the host gets there (one
+    // intake: the columns catch up on steps 0..s-1 in one pass per step, with L21 split
+    // again and inv(L11) rebuilt for each); then step s runs on all columns present.  Every
+    // column gets the same operations in the same order as in factor_and_solve's serial
+    // schedule whatever the intakes were, so the results are bit-identical to it.
     int factor_and_solve_ingest()
     {
         const int64_t nsb = (N + K - 1) / K;
+        const size_t nch = in_ev.size();
         int64_t ready = 0;   // columns [0, ready) are present and up to date with the steps issued
         size_t c = 0;
         for (int64_t s = 0; s < nsb; ++s) {
             const int64_t J = sb_start(s), KJ = sb_width(s), c1 = J + KJ;
-            while (c < in_ev.size() && (ready < c1 || s == nsb - 1)) {
+            size_t e = c;
+            while (e < nch && (in_bound[e] < c1 || s == nsb - 1 || cudaEventQuery(in_ev[e]) == cudaSuccess)) ++e;
+            if (e > c) {
                 if (cfg.verbose) {
-                    cudaEvent_t e;
-                    CHPL_CUDA(cudaEventCreate(&e));
-                    CHPL_CUDA(cudaEventRecord(e, s0));
-                    in_take.push_back(e);
+                    cudaEvent_t ev;
+                    CHPL_CUDA(cudaEventCreate(&ev));
+                    CHPL_CUDA(cudaEventRecord(ev, s0));
+                    in_take.push_back(ev);
                     in_step.push_back(s);
+                    in_first.push_back(c);
+                    in_last.push_back(e - 1);
                 }
-                CHPL_CUDA(cudaStreamWaitEvent(s0, in_ev[c], 0));
-                const int64_t a = in_bound[c], b = in_bound[c + 1];
+                for (size_t q = c; q < e; ++q) CHPL_CUDA(cudaStreamWaitEvent(s0, in_ev[q], 0));
+                const int64_t a = in_bound[c], b = in_bound[e];
                 for (int64_t t = 0; t < s; ++t) CHPL_TRY(apply_step(t, false, a, b - a));
                 ready = b;
-                ++c;
+                c = e;
             }
             CHPL_TRY(factor_superblock(s, 0));
             CHPL_TRY(apply_step(s, true, c1, ready - c1));
@@ -699,14 +705,15 @@ int run_impl(const chpl_hpl_config* cfg, const double* Ab, size_t ldab, int veri
     float ms_gen = 0.f, ms = 0.f;
     cudaEventElapsedTime(&ms_gen, g0, g1);
     cudaEventElapsedTime(&ms, t0, t1);
-    if (s.ingest && cfg->verbose) {   // when each chunk landed and when the factorization reached it
-        for (size_t c = 0; c < s.in_take.size() && c < s.in_ev.size(); ++c) {
+    if (s.ingest && cfg->verbose) {   // when each intake's last chunk landed and when the factorization reached it
+        for (size_t i = 0; i < s.in_take.size(); ++i) {
             float landed = 0.f, reached = 0.f;
-            cudaEventElapsedTime(&landed, t0, s.in_ev[c]);
-            cudaEventElapsedTime(&reached, t0, s.in_take[c]);
-            std::printf("INGEST: chunk %zu columns [%" PRId64 ", %" PRId64 ") landed %.1f ms, reached at step %" PRId64
-                        " %.1f ms\n",
-                        c, s.in_bound[c], s.in_bound[c + 1], landed, s.in_step[c], reached);
+            cudaEventElapsedTime(&landed, t0, s.in_ev[s.in_last[i]]);
+            cudaEventElapsedTime(&reached, t0, s.in_take[i]);
+            std::printf("INGEST: step %" PRId64 " takes chunks %zu..%zu, columns [%" PRId64 ", %" PRId64
+                        "): landed %.1f ms, reached %.1f ms\n",
+                        s.in_step[i], s.in_first[i], s.in_last[i], s.in_bound[s.in_first[i]],
+                        s.in_bound[s.in_last[i] + 1], landed, reached);
         }
         std::fflush(stdout);
     }

@@ -273,7 +273,6 @@ constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;       // double-buffered accumulator
 constexpr int SCRATCH_TILE = BM * BN;   // bytes per modulus per CTA
-constexpr int kPrefetchAhead = 8;       // k-blocks the producer's L2 prefetch runs ahead of its loads
 
 // Two forms of the kernel share one body:
 //   single: one CTA computes a 128 x 256 tile; it stages A 128 x 128 and
@@ -411,26 +410,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             int issued[STAGES];
             for (int s = 0; s < STAGES; ++s) issued[s] = -1;
             bool ok = true;
-            // L2 prefetch cursor, kPrefetchAhead k-blocks ahead of the loads: the first
-            // blocks of each modulus plane (and of the next tile) are warm in L2 when
-            // the ring reaches them instead of missing to HBM
-            int ptile = unit, pl = 0, pkb = 0, prow_a = 0, prow_b = 0;
-            auto pf_rows = [&]() {
-                int pmt, pnt;
-                tile_coords(p, ptile, pmt, pnt);
-                prow_a = pmt * F::TBM + (int)rank * BM;
-                prow_b = pnt * BN + (int)rank * F::B_ROWS;
-            };
-            auto pf_advance = [&]() {
-                if (++pkb < plane_kblocks(p, pl)) return;
-                pkb = 0;
-                if (++pl < L) return;
-                pl = 0;
-                ptile += nunits;
-                if (ptile < total) pf_rows();
-            };
-            if (ptile < total) pf_rows();
-            for (int i = 0; i < kPrefetchAhead && ptile < total; ++i) pf_advance();
             for (int tile = unit; tile < total && ok; tile += nunits) {
                 int mt, nt;
                 tile_coords(p, tile, mt, nt);
@@ -438,11 +417,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int rowB = nt * BN + (int)rank * F::B_ROWS;
                 for (int l = 0; l < L && ok; ++l)
                     for (int kb = 0; kb < plane_kblocks(p, l); ++kb) {
-                        if (ptile < total) {
-                            tma_prefetch_l2_2d(&tmA, pkb * BK, pl * p.planeA + prow_a);
-                            tma_prefetch_l2_2d(&tmB, pkb * BK, pl * p.rowsB + prow_b);
-                            pf_advance();
-                        }
                         if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag)) { ok = false; break; }
                         uint8_t* sa = smem + stage * STAGE_BYTES;
                         if (PAIR) {

@@ -188,7 +188,8 @@ struct Solver {
         size_t freeB = 0, totB = 0;
         CHPL_CUDA(cudaMemGetInfo(&freeB, &totB));
         const int npl = (int)((K + NB - 1) / NB);
-        const size_t ozbytes = 2 * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0) + oz1b * (cfg.lookahead ? 2 : 1);
+        const size_t ozbytes = (cfg.lookahead ? 2 : 1) * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0) +
+                               oz1b * (cfg.lookahead ? 2 : 1);
         const size_t pbytes = panel_work_bytes(N, NB);
         size_t linv_res = 0;   // residues of one inv(L) (A part, k = K)
         if (emu_trsm)
@@ -221,7 +222,11 @@ struct Solver {
             for (int p = 0; p < npl; ++p) CHPL_CUDA(cudaMalloc(&lw_old[p], laswp_work_bytes(NB)));
         }
         if (a_big) {
-            for (int b = 0; b < 2; ++b) CHPL_CUDA(cudaMalloc(&wA[b], a_big));
+            // the serial schedule orders every use of L21(s)'s residues before step s+1 splits
+            // L21(s+1): one buffer serves both parities
+            CHPL_CUDA(cudaMalloc(&wA[0], a_big));
+            if (cfg.lookahead) CHPL_CUDA(cudaMalloc(&wA[1], a_big));
+            else wA[1] = wA[0];
             CHPL_CUDA(cudaMalloc(&wAin, a_in));
             if (emu_trsm) {
                 for (int b = 0; b < 2; ++b) {
@@ -263,7 +268,7 @@ struct Solver {
             if (wLinv[b]) cudaFree(wLinv[b]);
         }
         for (int b = 0; b < 2; ++b) {
-            if (wA[b]) cudaFree(wA[b]);
+            if (wA[b] && !(b == 1 && wA[1] == wA[0])) cudaFree(wA[b]);
             for (void* p : lw[b]) if (p) cudaFree(p);
         }
         if (pwork) cudaFree(pwork);

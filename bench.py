@@ -277,9 +277,10 @@ def run_e2e_leg(a) -> None:
         W.generate(cfg.seed)
         hpl.run_host(hpl.Config(N=wn, NB=min(NB, wn), moduli=a.moduli), W, verify=True)
     walls, res = [], []
+    vcfg = hpl.Config(N=N, NB=NB, moduli=a.moduli, verbose=True)   # prints the copy / intake timeline
     for _ in range(a.steps):
         t = time.perf_counter()
-        r = hpl.run_host(cfg, S, verify=False)
+        r = hpl.run_host(vcfg, S, verify=False)
         walls.append(time.perf_counter() - t)
         res.append(r)
     chk = hpl.run_host(cfg, S, verify=True)     # untimed: the residual of this solve against the caller's [A | b]
@@ -304,6 +305,10 @@ def e2e_host(a, N: int, NB: int, fallback: dict) -> dict:
     try:
         p = subprocess.run(cmd, capture_output=True, text=True, timeout=1200)
         leg = json.loads(p.stdout.strip().splitlines()[-1]) if p.returncode == 0 and p.stdout.strip() else None
+        if leg is not None:   # the last timed call's chunk timeline (intake step, landed / reached ms)
+            lines = [ln[len("INGEST: "):] for ln in p.stdout.splitlines() if ln.startswith("INGEST: ")]
+            steps0 = [i for i, ln in enumerate(lines) if ln.startswith("step 0 ")]
+            leg["ingest"] = lines[steps0[-1]:] if steps0 else lines
         err = None if leg else f"child exited {p.returncode}: {(p.stderr or p.stdout).strip()[-300:]}"
     except (subprocess.TimeoutExpired, ValueError, IndexError) as ex:
         leg, err = None, f"{type(ex).__name__}: {ex}"
@@ -316,6 +321,7 @@ def e2e_host(a, N: int, NB: int, fallback: dict) -> dict:
            "resid": leg["resid"], "passed": leg["passed"], "x_equal_to_timed_steps": leg.get("x_equal_to_timed_steps"),
            "wall_s_per_step": sum(leg["wall_s"]) / len(leg["wall_s"]),
            "device_copy_and_solve_s_per_step": sum(leg["device_s"]) / len(leg["device_s"]),
+           "device_copy_and_solve_s": leg["device_s"], "ingest_timeline": leg.get("ingest"),
            "gpu_launches": leg["launches"],
            "note": "public host-buffer call chpl_hpl_run_host per step, wall clock: device allocation, [A|b] "
                    "host->device from pinned memory (streamed in column chunks while the factorization works on "

@@ -85,10 +85,16 @@ struct PhaseTimer {
 // 23.7 (N = 16384, a failure), 9.1 (32768), 4.8 (65536) and 2.3 (139264),
 // while N = 16384 without aggregation (k = NB = 1024) gave 3.9 in the same
 // time.  Below N = 65536 the panel dominates anyway, so nothing is aggregated.
+// From N = 131072 on, k = 6144: fewer modulus-plane switches per MAC in the
+// bulk GEMM outweigh the larger U12 product and inner updates (N = 139264,
+// NB = 1024: k = 4096 / 6144 / 8192 ran 13.76 / 13.51 / 13.63 s, residuals
+// 2.5 / 3.8 / 5.2).
 constexpr int64_t kAggMinN = 65536;
+constexpr int64_t kAggDeepN = 131072;
 static int auto_agg(int64_t N, int64_t NB)
 {
-    return N >= kAggMinN ? (int)std::max<int64_t>(1, 4096 / NB) : 1;
+    if (N < kAggMinN) return 1;
+    return (int)std::max<int64_t>(1, (N >= kAggDeepN ? 6144 : 4096) / NB);
 }
 
 struct Solver {

@@ -107,9 +107,9 @@ class Config:
 def single_config_from_env(N: int, env=None) -> Config:
     """chpl_single's configuration (src/chpl_single.cu:842-869, launcher defaults
     scripts/mpirun_chpl:71-76).  HPLS_AGG groups panels into super-blocks whose
-    trailing update runs with k = AGG * NB (0 = automatic: k = 4096 from
-    N = 65536 up, k = NB below, where deeper emulated updates cost residual
-    margin).  The matrix is chpl_single's cuRAND Philox one
+    trailing update runs with k = AGG * NB (0 = automatic: k = 6144 from
+    N = 131072 up, 4096 from 65536, k = NB below, where deeper emulated
+    updates cost residual margin).  The matrix is chpl_single's cuRAND Philox one
     (src/chpl_single.cu:73-80); HPLS_GEN=chpl (this build's switch) selects
     chpl_p2's SplitMix64 matrix instead."""
     env = os.environ if env is None else env

@@ -284,8 +284,9 @@ typedef struct chpl_hpl_config {
     int64_t chunk;      /* column chunk of the update (CHPL2D_G8_NT / HPLS_G8_CHUNK), 0 = auto */
     int lookahead;      /* depth-1 lookahead on a high-priority stream (1) or serial (0, default) */
     int agg;            /* HPLS_AGG: panels per super-block; the bulk update runs with k = agg * NB
-                           (src/chpl_single.cu:662); 0 = auto: k = 4096 for N >= 65536, else k = NB
-                           (the deeper emulated updates cost residual margin at small N) */
+                           (src/chpl_single.cu:662); 0 = auto: k = 6144 for N >= 131072, 4096 for
+                           N >= 65536, else k = NB (the deeper emulated updates cost residual margin
+                           at small N) */
     int reserve_sms;    /* SMs left to the lookahead chain while the bulk update runs; -1 = auto */
     int trsm_mode;      /* U12 of a super-block: 0 = auto, 1 = inv(L) * A12 through the emulated GEMM,
                            2 = FP64 triangular solve */

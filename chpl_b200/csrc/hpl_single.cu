@@ -12,7 +12,8 @@
 //           L21 split once per panel and reused across column chunks), or
 //           FP64 DGEMM when emulation is off.
 // Columns left of the panel are not interchanged: only U and the transformed
-// b are read afterwards (as src/chpl_p2.cu does, docs/DESIGN.md section 6.2).
+// b are read afterwards (as src/chpl_p2.cu does: its interchanges cover the
+// trailing columns only).
 //
 // Depth-1 lookahead (cfg.lookahead): the columns of panel k+1 are updated
 // first, on the high-priority stream sP, which then factors panel k+1 while

@@ -16,8 +16,8 @@ NB from the file (one GPU) or passes a copy whose P and Q lines carry -P and
 (scripts/mpirun_chpl:107-126), but they are this build's values, not the
 ones the reference tuned for GEMMul8 on H200:
 
-* one GPU: HPLS_NB 1024, HPLS_AGG 4 from N = 65536 up and 1 below (the
-  residual margin of 11 moduli), HPLS_BACKEND gemmul8, HPLS_G8_MODULI 11,
+* one GPU: HPLS_NB 1024, HPLS_AGG 6 from N = 131072 up, 4 from 65536 and 1
+  below (the residual margin of 11 moduli), HPLS_BACKEND gemmul8, HPLS_G8_MODULI 11,
   HPLS_G8_FAST 1, HPLS_G8_CHUNK 32768;
 * grids: CHPL2D_G8 1, CHPL2D_G8_MODULI 11, CHPL2D_G8_FAST 1.
 
@@ -92,7 +92,8 @@ def plan(P: int, Q: int, N: int | None, NB: int | None, input_path: str | None, 
         if N is None or N <= 0 or NB <= 0 or NB > N:
             raise LaunchError(f"bad N/NB ({N}, {NB})")
         exported["HPLS_NB"] = str(NB)
-        default("HPLS_AGG", max(1, 4096 // NB) if N >= 65536 else 1)
+        # the library's automatic depth (k = 6144 from N = 131072, 4096 from 65536)
+        default("HPLS_AGG", max(1, (6144 if N >= 131072 else 4096) // NB) if N >= 65536 else 1)
         default("HPLS_BACKEND", "gemmul8")
         default("HPLS_G8_MODULI", 11)
         default("HPLS_G8_FAST", 1)

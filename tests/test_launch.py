@@ -27,8 +27,9 @@ def _run(args, env=None):
 def test_single_gpu_defaults_follow_the_order():
     big = launch.plan(1, 1, 139264, None, None, {})
     assert big["exe"].endswith("chpl_single") and big["args"] == ["139264"]
-    assert big["env"] == {"HPLS_NB": "1024", "HPLS_AGG": "4", "HPLS_BACKEND": "gemmul8", "HPLS_G8_MODULI": "11",
+    assert big["env"] == {"HPLS_NB": "1024", "HPLS_AGG": "6", "HPLS_BACKEND": "gemmul8", "HPLS_G8_MODULI": "11",
                           "HPLS_G8_FAST": "1", "HPLS_G8_CHUNK": "32768"}
+    assert launch.plan(1, 1, 65536, None, None, {})["env"]["HPLS_AGG"] == "4"
     small = launch.plan(1, 1, 16384, None, None, {})
     assert small["env"]["HPLS_AGG"] == "1"          # 11 moduli keep their residual margin
     assert launch.plan(1, 1, 8192, 512, None, {})["env"]["HPLS_NB"] == "512"
@@ -89,7 +90,7 @@ def test_rejects_both_inputs_and_missing_file(tmp_path):
 def test_dry_run_cli():
     r = _run(["-P", "1", "-Q", "1", "-N", "139264", "--dry-run"])
     assert r.returncode == 0, r.stderr
-    assert "HPLS_AGG=4" in r.stdout and r.stdout.strip().splitlines()[-1].endswith("chpl_single 139264")
+    assert "HPLS_AGG=6" in r.stdout and r.stdout.strip().splitlines()[-1].endswith("chpl_single 139264")
     r = _run(["-P", "2", "-Q", "2", "-N", "278528", "--dry-run"])
     assert r.returncode == 0 and "CHPL2D_G8=1" in r.stdout and "278528" in r.stdout
     r = _run(["-P", "4", "-Q", "4", "-N", "65536"])

@@ -293,7 +293,8 @@ typedef struct chpl_hpl_config {
     int panel_mode;     /* 0 = this library's FP64 panel kernel, 1 = cuSOLVER getrf (comparison) */
     uint64_t seed;      /* 42 */
     double threshold;   /* HPL.dat line 13 (16.0) */
-    int verbose;        /* print progress lines */
+    int verbose;        /* print the memory plan (MEM PLAN) and, for a host system streamed in, each
+                           intake of column chunks (INGEST: step, columns, landed / reached ms) */
     int generator;      /* CHPL_GEN_CHPL (default; chpl_p2's matrix) or CHPL_GEN_PHILOX (chpl_single's matrix);
                            one-GPU runs only, the grid driver generates with CHPL_GEN_CHPL as chpl_p2 does */
 } chpl_hpl_config;

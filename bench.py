@@ -276,7 +276,7 @@ def run_e2e_leg(a) -> None:
     with hpl.HostSystem(wn) as W:       # warm-up at a small order: module load, allocator
         W.generate(cfg.seed)
         hpl.run_host(hpl.Config(N=wn, NB=min(NB, wn), moduli=a.moduli), W, verify=True)
-    hpl.run_host(cfg, S, verify=False)  # and one untimed call at the full order (the first pass over [A|b] is slower)
+    hpl.run_host(cfg, S, verify=False)  # and one untimed call at the full order (a first one ran ~2 s slower)
     walls, res = [], []
     vcfg = hpl.Config(N=N, NB=NB, moduli=a.moduli, verbose=True)   # prints the copy / intake timeline
     for _ in range(a.steps):

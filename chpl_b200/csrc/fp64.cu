@@ -486,8 +486,11 @@ int trtri_pow2(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double*
 }
 
 // X = inv(L) for X = I on entry.  n = kLeaf * 2^q: level-batched (trtri_pow2);
-// otherwise the largest such n1 < n first, X22 = inv(L22) recursively, then
-// X21 = -inv(L22) (L21 X11) as a product and a solve.
+// otherwise the largest such n1 < n first and X22 = inv(L22) recursively, then
+// X21 = -X22 (L21 X11).  With n2 >= n1 / 4 that is products only, in column
+// blocks of n2: T = L21 X11(:, blk) goes to X's zero upper block X(0:n2,
+// n1:n1+n2), X21(:, blk) = -X22 T, and the block is zeroed again at the end;
+// a thinner n2 uses X21 = -L21 X11 followed by the solve with L22.
 int trtri_rec(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* X, int64_t ldx)
 {
     if (n <= kLeaf) return trsm_rec(st, n, n, L, ldl, X, ldx);
@@ -497,8 +500,20 @@ int trtri_rec(cudaStream_t st, int64_t n, const double* L, int64_t ldl, double* 
     const int64_t n2 = n - n1;
     CHPL_TRY(trtri_pow2(st, n1, L, ldl, X, ldx));
     CHPL_TRY(trtri_rec(st, n2, L + n1 + n1 * ldl, ldl, X + n1 + n1 * ldx, ldx));
-    CHPL_TRY(dgemm(st, n2, n1, n1, -1.0, L + n1, ldl, X, ldx, 0.0, X + n1, ldx));
-    return trsm_rec(st, n2, n1, L + n1 + n1 * ldl, ldl, X + n1, ldx);
+    if (4 * n2 < n1) {
+        CHPL_TRY(dgemm(st, n2, n1, n1, -1.0, L + n1, ldl, X, ldx, 0.0, X + n1, ldx));
+        return trsm_rec(st, n2, n1, L + n1 + n1 * ldl, ldl, X + n1, ldx);
+    }
+    double* T = X + n1 * ldx;   // rows 0..n2-1 of the zero block right of X11 (n2 <= n1)
+    for (int64_t j0 = 0; j0 < n1; j0 += n2) {
+        const int64_t w = std::min(n2, n1 - j0);
+        CHPL_TRY(dgemm(st, n2, w, n1 - j0, 1.0, L + n1 + j0 * ldl, ldl, X + j0 + j0 * ldx, ldx, 0.0, T, ldx));
+        CHPL_TRY(dgemm(st, n2, w, n2, -1.0, X + n1 + n1 * ldx, ldx, T, ldx, 0.0, X + n1 + j0 * ldx, ldx));
+    }
+    const unsigned g = (unsigned)std::min<long long>((n2 * n2 + 255) / 256, 148LL * 32);
+    zero_blocks_kernel<<<g, 256, 0, st>>>(T, (long long)ldx, (long long)n2, 0LL, 1LL);
+    CHPL_CUDA(cudaGetLastError());
+    return CHPL_OK;
 }
 
 int64_t trsm_count(int64_t n)
@@ -559,7 +574,9 @@ int64_t dtrtri_launches(int64_t n)
     int64_t n1 = kLeaf, levels = 0;
     while (2 * n1 <= n) { n1 *= 2; ++levels; }   // n1 = kLeaf * 2^levels <= n
     if (n1 == n) return 1 + 3 * levels;
-    return (1 + 3 * levels) + dtrtri_launches(n - n1) + 1 + trsm_count(n - n1);
+    const int64_t n2 = n - n1;
+    const int64_t rest = 4 * n2 < n1 ? 1 + trsm_count(n2) : 2 * ((n1 + n2 - 1) / n2) + 1;
+    return (1 + 3 * levels) + dtrtri_launches(n2) + rest;
 }
 
 int dtrsv_unn(cudaStream_t st, int64_t n, const double* U, int64_t ldu, double* x, double* work)

@@ -122,7 +122,7 @@ def test_dtrsm_inverse_against_identity(cuda):
     assert np.array_equal(np.triu(Li, 1), np.zeros((n, n)))
 
 
-@pytest.mark.parametrize("n", [1, 64, 65, 200, 1024, 2112, 3000, 4096])
+@pytest.mark.parametrize("n", [1, 64, 65, 200, 1024, 2112, 3000, 4096, 6144])
 def test_dtrtri_inverse(cuda, n):
     """inv(L) level by level (64 * 2^q orders: every pair of a level in one
     batched launch) and recursively for other orders: L X = I to a few ulps

@@ -133,16 +133,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
-// L2 prefetch of the tile a tma_load_2d with the same map and coordinates would
-// copy (no shared memory written, no barrier)
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y)
-{
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(tmap)),
-                 "r"(x), "r"(y)
-                 : "memory");
-}
-
 // ---- tcgen05 -------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols)
 {

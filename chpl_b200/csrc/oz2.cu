@@ -273,7 +273,6 @@ constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 2 * BN;       // double-buffered accumulator
 constexpr int SCRATCH_TILE = BM * BN;   // bytes per modulus per CTA
-constexpr int kPlanePrefetchLead = 6;   // k-blocks before a plane's end at which the next plane is prefetched
 
 // Two forms of the kernel share one body:
 //   single: one CTA computes a 128 x 256 tile; it stages A 128 x 128 and
@@ -297,7 +296,6 @@ struct GemmParams {
     int m, n;
     int mtiles, ntiles, kblocks;
     int kstep;          // > 0: plane l stops after (l + 1) * kstep bytes of K (the rest of its B rows is zero)
-    int plane_prefetch;               // k-blocks of the next plane the producer prefetches into L2 (0: none)
     int magic[kMaxModuli];            // ceil(2^32 / m_l): the epilogue's residue estimate
     unsigned long long crt_bias;      // -128 * sum_l v_l mod 2^64: removes the residues' +128 bias
     int rowsA, rowsB;   // padded rows per modulus plane in the residue buffers
@@ -419,25 +417,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int rowB = nt * BN + (int)rank * F::B_ROWS;
                 for (int l = 0; l < L && ok; ++l)
                     for (int kb = 0; kb < plane_kblocks(p, l); ++kb) {
-                        if (p.plane_prefetch > 0 && kb == max(0, plane_kblocks(p, l) - kPlanePrefetchLead)) {
-                            // warm L2 with the first blocks of the next plane (or of the next tile's first)
-                            int nl = l + 1, ntile = tile, nra = rowA, nrb = rowB;
-                            if (nl == L) {
-                                nl = 0;
-                                ntile = tile + nunits;
-                                if (ntile < total) {
-                                    int nmt, nnt;
-                                    tile_coords(p, ntile, nmt, nnt);
-                                    nra = nmt * F::TBM + (int)rank * BM;
-                                    nrb = nnt * BN + (int)rank * F::B_ROWS;
-                                }
-                            }
-                            if (ntile < total)
-                                for (int q = 0; q < p.plane_prefetch && q < plane_kblocks(p, nl); ++q) {
-                                    tma_prefetch_l2_2d(&tmA, q * BK, nl * p.planeA + nra);
-                                    tma_prefetch_l2_2d(&tmB, q * BK, nl * p.rowsB + nrb);
-                                }
-                        }
                         if (!mbar_wait(&empty[stage], ph ^ 1u, abort_flag)) { ok = false; break; }
                         uint8_t* sa = smem + stage * STAGE_BYTES;
                         if (PAIR) {
@@ -858,7 +837,6 @@ int gemm_launch(cudaStream_t st, int mode, size_t m, size_t n, size_t kPad, unsi
     p.mode = mode;
     p.group_m = pair ? 8 : 16;
     if (const char* g = std::getenv("CHPL_OZ2_GROUP_M")) p.group_m = std::max(1, std::atoi(g));
-    if (const char* g = std::getenv("CHPL_OZ2_PLANE_PREFETCH")) p.plane_prefetch = std::max(0, std::min(8, std::atoi(g)));
     p.C = C;
     p.ldc = (long long)ldc;
     p.P = P;

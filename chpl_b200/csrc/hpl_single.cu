@@ -198,9 +198,10 @@ struct Solver {
         const size_t ozbytes = (cfg.lookahead ? 2 : 1) * a_big + a_in + rest0 + (cfg.lookahead ? restP : 0) +
                                oz1b * (cfg.lookahead ? 2 : 1);
         const size_t pbytes = panel_work_bytes(N, NB);
-        size_t linv_res = 0;   // residues of one inv(L) (A part, k = K)
+        size_t linv_res = 0, linv_tot = 0;   // residues of one inv(L) (A part, k = K)
         if (emu_trsm)
-            CHPL_TRY(chpl_oz2_worksize((size_t)K, 256, (size_t)K, (unsigned)cfg.moduli, 1, 0, &tot, &linv_res, nullptr));
+            CHPL_TRY(chpl_oz2_worksize((size_t)K, 256, (size_t)K, (unsigned)cfg.moduli, 1, 0, &linv_tot, &linv_res,
+                                       nullptr));
         const size_t linv_bytes = emu_trsm ? (size_t)K * K * sizeof(double) + linv_res : 0;
         const size_t need = bytesA + ozbytes + pbytes + (ingest ? 3 : 2) * (npl * laswp_work_bytes(NB) + linv_bytes) +
                             (size_t)(3 * N + 64) * 8 + ((size_t)768 << 20);

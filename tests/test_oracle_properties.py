@@ -121,3 +121,38 @@ def test_shift_bits_fit_the_crt_range(L):
     """alpha + beta < log2(M) - 1: the Cauchy-Schwarz bound 2^(alpha+beta) < M/2."""
     a, b = oracle.oz2_shift_bits(L, 4096)
     assert 2 ** (a + b) < oracle.oz2_constants(L)["M"] // 2
+
+
+# ---------------------------------------------------------------- Ozaki scheme I (oracle.oz1_gemm)
+@SETTINGS
+@given(scaled_matrix(max_rows=5, max_k=40), st.integers(1, 5), st.integers(0, 2**31 - 1))
+def test_oz1_digits_and_products_are_exact(A, n, seed):
+    """The Ozaki-I restatement's facts, in exact rational arithmetic: a scaled
+    entry x in (-1, 1) is sum_p t_p 128^-(p+1) + r 128^-6 with integer digits
+    t_p in [-128, 127] and |r| <= 1; the diagonal sums of digit products the
+    float64 BLAS forms are the exact integers; and the emulated product keeps
+    every entry within k 2^-40 of its row x column scale."""
+    from fractions import Fraction
+    m, k = A.shape
+    B = np.random.default_rng(seed).uniform(-0.5, 0.5, (k, n))
+    ea = np.frexp(np.max(np.abs(A), axis=1))[1]
+    xa = np.ldexp(A, -ea[:, None])
+    assert np.all(np.abs(xa) < 1.0)
+    da = oracle._oz1_digits(xa)
+    for p in range(oracle.OZ1_SLICES):
+        assert np.all(da[p] == np.rint(da[p])) and np.all((da[p] >= -128) & (da[p] <= 127))
+    # the remainder after six digits, recomputed exactly
+    for i in range(m):
+        for h in range(k):
+            x = Fraction(float(xa[i, h]))
+            head = sum(Fraction(int(da[p][i, h])) / 128 ** (p + 1) for p in range(oracle.OZ1_SLICES))
+            assert abs(x - head) * 128 ** oracle.OZ1_SLICES <= 1
+    eb = np.frexp(np.max(np.abs(B), axis=0))[1]
+    db = oracle._oz1_digits(np.ldexp(B, -eb[None, :]))
+    for d in range(oracle.OZ1_SLICES):
+        P = np.hstack(da[:d + 1]) @ np.vstack(db[d::-1])
+        Q = sum(da[p].astype(np.int64) @ db[d - p].astype(np.int64) for p in range(d + 1))
+        assert np.array_equal(P.astype(np.int64), Q)
+    got = oracle.oz1_gemm(A, B, np.zeros((m, n)), alpha=1.0, beta=0.0)
+    bound = k * 2.0 ** -40 * np.ldexp(1.0, ea)[:, None] * np.ldexp(1.0, eb)[None, :]
+    assert np.all(np.abs(got - A @ B) <= bound + 1e-300)

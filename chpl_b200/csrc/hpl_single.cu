@@ -495,6 +495,17 @@ struct Solver {
         return cfg.lookahead && reserve > 0 && (N - c2) >= 8 * K;
     }
 
+    // x = U^-1 b': the back substitution on column N, on s0
+    int back_solve()
+    {
+        PhaseTimer::Rec r;
+        CHPL_TRY(clk.begin(s0, PH_SOLVE, r));
+        CHPL_TRY(dtrsv_unn(s0, N, A, ld, at(0, N), xwork));
+        n_launch += dtrsv_launches(N);
+        CHPL_TRY(clk.end(s0, r));
+        return CHPL_OK;
+    }
+
     // Enqueue [A | b] from host memory (leading dimension ldab) on the copy stream in column
     // chunks of 2K columns (two super-blocks; the last chunk ends at column N), each followed
     // by its event.  The copies start once `start` has been reached on s0.
@@ -580,12 +591,7 @@ struct Solver {
             CHPL_TRY(factor_superblock(s, 0));
             CHPL_TRY(apply_step(s, true, c1, ready - c1));
         }
-        PhaseTimer::Rec r;
-        CHPL_TRY(clk.begin(s0, PH_SOLVE, r));
-        CHPL_TRY(dtrsv_unn(s0, N, A, ld, at(0, N), xwork));
-        n_launch += dtrsv_launches(N);
-        CHPL_TRY(clk.end(s0, r));
-        return CHPL_OK;
+        return back_solve();
     }
 
     int factor_and_solve()
@@ -616,12 +622,7 @@ struct Solver {
             CHPL_TRY(update(s0, w0, wA[s & 1], !a_split && K2 == 0, c1, J, KJ, c2 + K2, ncols - c2 - K2, cap_bulk));
         }
         CHPL_TRY(wait(s0, sP));
-        PhaseTimer::Rec r;
-        CHPL_TRY(clk.begin(s0, PH_SOLVE, r));
-        CHPL_TRY(dtrsv_unn(s0, N, A, ld, at(0, N), xwork));
-        n_launch += dtrsv_launches(N);
-        CHPL_TRY(clk.end(s0, r));
-        return CHPL_OK;
+        return back_solve();
     }
 
     void gemm_stats(chpl_hpl_result* res)

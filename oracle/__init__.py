@@ -329,6 +329,13 @@ def ref_single_matgen_path() -> str | None:
     return so if os.path.exists(so) else None
 
 
+def ref_oz1_path() -> str | None:
+    """Path of oracle/_ref/libref_oz1.so (chpl_single's own Ozaki-I scale,
+    slice and reconstruction kernels, sm_100a), or None if it was never built."""
+    so = os.path.join(_REF, "libref_oz1.so")
+    return so if os.path.exists(so) else None
+
+
 def ref_resolve_seq(piv: np.ndarray, base: int) -> tuple[np.ndarray, dict]:
     """The reference's resolve_seq: (top, {row >= base+n: original row})."""
     L = ref_host()

@@ -3,7 +3,7 @@
 The reference (Koyingtw/CHPL) cannot be built as a whole here: its CMake
 build needs MPI and the GEMMul8 submodule, which is empty.  Four pieces of it
 are self-contained, though, and are what parity of this project's generator,
-interchange planning and residual hangs on.  This recipe cuts them out of the
+interchange planning, residual and Ozaki-I engine hangs on.  This recipe cuts them out of the
 reference checkout (located by CHPL_REFERENCE_ROOT) by pattern, writes them
 verbatim into oracle/_ref/ (git-ignored: reference source never enters this
 repository's history) and compiles them with this project's harnesses:
@@ -16,9 +16,13 @@ repository's history) and compiles them with this project's harnesses:
                                         run_case (norms and the formula)
   single_matgen.inc  src/chpl_single.cu hs_rand + matgen_kernel: chpl_single's
                                         cuRAND Philox generator
+  single_oz1.inc     src/chpl_single.cu ozrowscale_kernel .. ozrecon_kernel:
+                                        chpl_single's Ozaki-I scales, digit
+                                        slices and reconstruction
 
   oracle/_ref/libref_host.so           g++ on oracle/ref_host.cpp (the first three)
   oracle/_ref/libref_single_matgen.so  nvcc (sm_100a) on oracle/ref_single_matgen.cu
+  oracle/_ref/libref_oz1.so            nvcc (sm_100a) on oracle/ref_oz1.cu
 
 oracle/_ref/manifest.json records the file and line range of each fragment.
 The built libraries travel with the repository snapshot to a GPU machine
@@ -100,6 +104,10 @@ def _extract(root: str) -> dict:
     s, _ = _cut(L, r"^__device__ __forceinline__ double hs_rand\(", _closing_brace)
     _, e = _cut(L, r"^__global__ void matgen_kernel\(", _closing_brace)
     write("single_matgen.inc", "src/chpl_single.cu", s, e)
+    # chpl_single's Ozaki-I kernels: ozrowscale_kernel through the end of ozrecon_kernel
+    s, _ = _cut(L, r"^__global__ void ozrowscale_kernel\(", _closing_brace)
+    _, e = _cut(L, r"^__global__ void ozrecon_kernel\(", _closing_brace)
+    write("single_oz1.inc", "src/chpl_single.cu", s, e)
     with open(os.path.join(OUT, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=1)
     return manifest
@@ -119,9 +127,10 @@ def build(force: bool = False) -> bool:
         return False
     host_so = os.path.join(OUT, "libref_host.so")
     dev_so = os.path.join(OUT, "libref_single_matgen.so")
-    deps = [os.path.join(HERE, f) for f in ("ref_build.py", "ref_host.cpp", "ref_single_matgen.cu")]
+    oz1_so = os.path.join(OUT, "libref_oz1.so")
+    deps = [os.path.join(HERE, f) for f in ("ref_build.py", "ref_host.cpp", "ref_single_matgen.cu", "ref_oz1.cu")]
     newest = max(os.path.getmtime(d) for d in deps)
-    if not force and all(os.path.exists(p) and os.path.getmtime(p) >= newest for p in (host_so, dev_so)):
+    if not force and all(os.path.exists(p) and os.path.getmtime(p) >= newest for p in (host_so, dev_so, oz1_so)):
         return True
     _extract(reference_root())
     _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-I", OUT,
@@ -129,6 +138,9 @@ def build(force: bool = False) -> bool:
     _run([os.path.join(CUDA, "bin", "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
           "-shared", "-Xcompiler", "-fPIC", "-cudart", "shared", "-I", OUT, os.path.join(HERE, "ref_single_matgen.cu"),
           "-o", dev_so])
+    _run([os.path.join(CUDA, "bin", "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+          "-shared", "-Xcompiler", "-fPIC", "-cudart", "shared", "-I", OUT, os.path.join(HERE, "ref_oz1.cu"),
+          "-o", oz1_so])
     return True
 
 

@@ -75,3 +75,57 @@ def test_philox_solve_agrees_with_lapack(cuda):
         x = r.x
         assert np.linalg.norm(x - x_ref) / np.linalg.norm(x_ref) < tol, emulate
         assert abs(r.resid - oracle.hpl_residual_from(Ab, x)) <= 1e-6 * max(1.0, r.resid) + 1e-3
+
+
+# ---------------------------------------------------------------- chpl_single's Ozaki-I kernels
+_OZ1_SO = oracle.ref_oz1_path()
+
+
+@pytest.mark.skipif(_OZ1_SO is None, reason="oracle/_ref not built (no reference checkout)")
+@pytest.mark.parametrize("m,n,k", [(300, 200, 257), (1000, 64, 1024), (129, 777, 96)])
+def test_oz1_engine_equals_reference_kernels(cuda, m, n, k):
+    """C -= A B through the reference's own Ozaki-I kernels (row / column
+    scales, digit slices and reconstruction of src/chpl_single.cu:147-236,
+    compiled from the reference checkout into oracle/_ref/libref_oz1.so) with
+    the six diagonal products of their digits formed exactly on the host (the
+    reference forms them with cuBLASLt int8 GEMMs: exact integers either way)
+    equals this library's chpl_oz1_gemm bit for bit."""
+    S = 6
+    R = ctypes.CDLL(_OZ1_SO)
+    vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+    R.ref_oz1_prepare.argtypes = [vp, sz, i32, i32, vp, sz, i32, i32, vp, vp, vp, vp, vp, vp]
+    R.ref_oz1_recon.argtypes = [vp, sz, i32, i32, vp, vp, vp, vp, vp, vp, i32, vp, vp]
+    rng = np.random.default_rng(m + n + k)
+    A = rng.uniform(-1, 1, (m, k)) * np.exp2(rng.integers(-30, 30, m))[:, None]
+    B = rng.uniform(-1, 1, (k, n))
+    C = rng.uniform(-1, 1, (m, n))
+    dA = torch.from_numpy(np.ascontiguousarray(A.T)).cuda()      # column-major, ld = m
+    dB = torch.from_numpy(np.ascontiguousarray(B.T)).cuda()      # ld = k
+    f64 = dict(dtype=torch.float64, device="cuda")
+    rinv, rsc, cinv, csc = (torch.empty(x, **f64) for x in (m, m, n, n))
+    SA = torch.empty(m * S * k, dtype=torch.int8, device="cuda")
+    SB = torch.empty(n * S * k, dtype=torch.int8, device="cuda")
+    assert R.ref_oz1_prepare(dA.data_ptr(), m, m, k, dB.data_ptr(), k, n, S, rinv.data_ptr(), rsc.data_ptr(),
+                             cinv.data_ptr(), csc.data_ptr(), SA.data_ptr(), SB.data_ptr()) == 0
+    sa = SA.cpu().numpy().reshape(m, S, k).astype(np.float64)          # [i][p][h]
+    sb = SB.cpu().numpy().reshape(n, S, k)[:, ::-1, :].astype(np.float64)   # [j][q][h], q ascending
+    D = []
+    for d in range(S):   # integers below 2^53 in every partial sum: exact in float64
+        P = sum(sa[:, p, :] @ sb[:, d - p, :].T for p in range(d + 1))
+        D.append(torch.from_numpy(np.ascontiguousarray(P.T).astype(np.int32)).cuda())   # column-major m x n
+    dC = torch.from_numpy(np.ascontiguousarray(C.T)).cuda()
+    assert R.ref_oz1_recon(dC.data_ptr(), m, m, n, *[x.data_ptr() for x in D], S, rsc.data_ptr(),
+                           csc.data_ptr()) == 0
+    ref = dC.cpu().numpy().T
+    # this library's engine on the same inputs
+    L = _lib.load()
+    w = ctypes.c_size_t()
+    _lib.check(L.chpl_oz1_worksize(m, n, k, ctypes.byref(w)), "chpl_oz1_worksize")
+    work = torch.empty(w.value, dtype=torch.uint8, device="cuda")
+    dC2 = torch.from_numpy(np.ascontiguousarray(C.T)).cuda()
+    _lib.check(L.chpl_oz1_gemm(None, m, n, k, -1.0, dA.data_ptr(), m, dB.data_ptr(), k, 1.0, dC2.data_ptr(), m,
+                               work.data_ptr()), "chpl_oz1_gemm")
+    torch.cuda.synchronize()
+    got = dC2.cpu().numpy().T
+    assert np.array_equal(got.view(np.uint64), ref.view(np.uint64))
+    assert np.array_equal(got.view(np.uint64), oracle.oz1_gemm(A, B, C).view(np.uint64))

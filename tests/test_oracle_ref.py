@@ -32,11 +32,12 @@ def _ref_matgen(m, n, row0=0, col0=0, ncg=None, seed=42):
 
 def test_fragments_were_cut_from_the_expected_functions():
     man = json.load(open(os.path.join(os.path.dirname(oracle.__file__), "_ref", "manifest.json")))
-    assert set(man) == {"chpl_elem.inc", "resolve_seq.inc", "residual.inc", "single_matgen.inc"}
+    assert set(man) == {"chpl_elem.inc", "resolve_seq.inc", "residual.inc", "single_matgen.inc", "single_oz1.inc"}
     assert man["chpl_elem.inc"]["file"] == "src/chpl_p2.cu"
     assert man["resolve_seq.inc"]["file"] == "src/chpl_p2.cu"
     assert man["residual.inc"]["file"] == "src/chpl_single.cu"
     assert man["single_matgen.inc"]["file"] == "src/chpl_single.cu"
+    assert man["single_oz1.inc"]["file"] == "src/chpl_single.cu"
     for v in man.values():
         a, b = v["lines"]
         assert 0 < a < b

@@ -132,3 +132,11 @@ def test_oz1_degenerate_and_limits(cuda):
                            a.data_ptr()) == _lib.CHPL_ERR_UNSUPPORTED
     assert L.chpl_oz1_gemm(None, 4, 4, 4, -1.0, a.data_ptr(), 4, a.data_ptr(), 4, 1.0, a.data_ptr(), 4,
                            None) == _lib.CHPL_ERR_WORKSPACE
+
+
+def test_oz1_golden_fixture(cuda):
+    """The committed fixture (tests/golden/oz1_m48_n40_k200.npz), bit for bit."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "oz1_m48_n40_k200.npz"))
+    assert _same(_oz1(g["A"], g["B"], g["C"]), g["update"])
+    assert _same(_oz1(g["A"], g["B"], g["C"], alpha=1.0, beta=0.0), g["product"])

@@ -195,3 +195,12 @@ def test_emulated_lu_residual_passes():
     src/chpl_single.cu:931-948) holds for the restated method at 12 moduli."""
     x, _, _ = oracle.hpl_solve(512, 64, L=12)
     assert oracle.hpl_residual(x, 512) < 16.0
+
+
+def test_oz1_golden_fixture():
+    """The Ozaki-I restatement reproduces its committed fixture bit for bit."""
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "oz1_m48_n40_k200.npz"))
+    upd = oracle.oz1_gemm(g["A"], g["B"], g["C"])
+    prod = oracle.oz1_gemm(g["A"], g["B"], None, alpha=1.0, beta=0.0)
+    assert np.array_equal(upd.view(np.uint64), g["update"].view(np.uint64))
+    assert np.array_equal(prod.view(np.uint64), g["product"].view(np.uint64))
